@@ -1,0 +1,121 @@
+/*
+ * C ABI of the B200 (sm_100a) sparse-MLA attention library.
+ *
+ * Sparse MLA in the NoPE geometry (qk_rope_head_dim = 0, head size =
+ * kv_lora_rank = 512): every query token attends only to the top-k rows of a
+ * flat latent KV pool named by its index list, and an index < 0 is the only
+ * mask. The same row serves as key and value (absorbed MLA).
+ *
+ * Plain pointers, sizes and scalars only; no framework types cross this
+ * boundary. All device pointers must be 16-byte aligned and the tensors
+ * row-major contiguous. The stream argument is a cudaStream_t passed as void*.
+ *
+ * Build: libglm53_sparse_mla.so (nvcc, -gencode arch=compute_100a,code=sm_100a).
+ */
+#ifndef GLM53_SPARSE_MLA_H_
+#define GLM53_SPARSE_MLA_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes returned by every entry point. */
+enum glm53_status {
+  GLM53_OK = 0,
+  GLM53_ERR_RANK = 1,          /* wrong tensor rank / shape mismatch            */
+  GLM53_ERR_HEAD_DIM = 2,      /* head size or kv width is not 512              */
+  GLM53_ERR_HEADS = 3,         /* heads per launch not in {8, 16, 32, 64}        */
+  GLM53_ERR_TOPK = 4,          /* top-k not a multiple of 32, or too large       */
+  GLM53_ERR_DTYPE = 5,         /* kv dtype is neither bf16 nor fp8_e4m3          */
+  GLM53_ERR_ALIGN = 6,         /* a pointer is null or not 16-byte aligned       */
+  GLM53_ERR_SPLITS = 7,        /* explicit split count not in {0, 1, 2, 4, 8}    */
+  GLM53_ERR_CUDA = 8,          /* a CUDA runtime call failed                     */
+  GLM53_ERR_DEVICE = 9         /* current device is not sm_100                   */
+};
+
+/* KV pool element type. */
+enum glm53_kv_dtype {
+  GLM53_KV_BF16 = 0,
+  GLM53_KV_FP8_E4M3 = 1
+};
+
+/* Bits of the device-side status word (see glm53_sparse_mla_device_status). */
+enum glm53_device_status_bits {
+  GLM53_DEV_TIMEOUT = 1u,      /* a pipeline wait gave up after its time limit   */
+  GLM53_DEV_BAD_INDEX = 2u     /* an index >= kv_rows was seen and masked out    */
+};
+
+/*
+ * Sparse-MLA forward.
+ *
+ *   q        [T, H, 512]  bf16
+ *   kv       [R, 512]     bf16 or fp8_e4m3 (per-tensor scale kv_scale)
+ *   indices  [T, topk]    int32 physical row ids into kv, < 0 = masked
+ *   out      [T, H, 512]  bf16, written in place (caller-owned)
+ *   lse      [T, H]       fp32 log2-space log-sum-exp, or NULL. A fully masked
+ *                         (token, head) gets -inf and an all-zero output row.
+ *
+ * sm_scale is the natural-log softmax scale (the kernel multiplies by log2 e).
+ * kv_scale multiplies dequantised fp8 values; it is ignored for bf16.
+ * splits: 0 = choose automatically; 1, 2, 4 or 8 = split each token's top-k
+ * list across that many CTAs of one thread-block cluster.
+ * H must be 8, 16, 32 or 64; head_dim and the kv width must be 512; topk must
+ * be a multiple of 32 and at most 16384. T == 0 is a no-op.
+ *
+ * Replaces the host launcher `sparse_fwd(q, kv, indices, sm_scale, kv_scale,
+ * out)` of the reference (csrc/sparse_mla.cu:455-498) and its launch helper
+ * (csrc/sparse_mla.cu:434-453); the lse output has no counterpart there and
+ * follows the fp32 oracle's log2 convention (tests/reference.py:71-73).
+ * Launch is asynchronous on `stream`; no host synchronisation, no allocation.
+ */
+int glm53_sparse_mla_fwd(const void* q, const void* kv, const int32_t* indices, void* out,
+                         float* lse, int64_t T, int64_t H, int64_t head_dim, int64_t kv_rows,
+                         int64_t kv_width, int64_t topk, int kv_dtype, float sm_scale,
+                         float kv_scale, int splits, void* stream);
+
+/*
+ * Argument validation alone, with no CUDA call: returns the status that
+ * glm53_sparse_mla_fwd would return before launching. Mirrors the TORCH_CHECKs
+ * of the reference host op (csrc/sparse_mla.cu:457-470, 488-496).
+ */
+int glm53_sparse_mla_check(int64_t T, int64_t H, int64_t head_dim, int64_t kv_rows,
+                           int64_t kv_width, int64_t topk, int kv_dtype, int splits);
+
+/* Split count the launcher would use for this shape on the current device. */
+int glm53_sparse_mla_auto_splits(int64_t T, int64_t topk, int sm_count);
+
+/*
+ * Raise the kernels' dynamic shared-memory limit on the current device. Called
+ * implicitly by the first glm53_sparse_mla_fwd on each device; call it
+ * explicitly before a CUDA graph capture if the first launch would otherwise
+ * happen inside the capture. Replaces the function-local static of
+ * csrc/sparse_mla.cu:440-444.
+ */
+int glm53_sparse_mla_prepare(void);
+
+/*
+ * Read (and optionally clear) the device status word of the current device:
+ * the OR of glm53_device_status_bits raised by kernels since the last clear.
+ * Synchronises the device. Not part of the hot path.
+ */
+int glm53_sparse_mla_device_status(uint32_t* status, int clear);
+
+/* Human-readable text for a glm53_status code. */
+const char* glm53_sparse_mla_strerror(int code);
+
+/*
+ * Gather-only bandwidth probe: copies the rows named by `indices` ([T, topk],
+ * < 0 skipped) of a bf16 [R, 512] pool into shared memory and discards them.
+ * Measures the achievable indexed-gather rate that bounds the attention
+ * kernel. Replaces the bench-only probe bench/gather_roof.cu:13-55.
+ */
+int glm53_gather_roof(const void* kv, const int32_t* indices, int64_t T, int64_t topk,
+                      int64_t kv_rows, void* sink, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GLM53_SPARSE_MLA_H_ */

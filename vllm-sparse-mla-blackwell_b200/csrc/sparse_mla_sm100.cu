@@ -1,0 +1,786 @@
+// Sparse MLA (NoPE: head size = kv_lora_rank = 512, no rope tail) for B200,
+// sm_100a only. One launch serves prefill and decode tokens alike: each query
+// token attends to the rows of a flat latent KV pool named by its top-k index
+// list; an index < 0 is the only mask (causality belongs to the indexer).
+//
+// Work decomposition
+//   grid.x = T * splits. The `splits` CTAs of one token form a thread-block
+//   cluster and each takes a contiguous chunk of the token's index list; their
+//   partial results are merged through distributed shared memory at the end,
+//   so no global scratch and no second launch are needed.
+//
+// Per CTA (288 threads, one CTA per SM, ~219 KB shared memory)
+//   warps 0-3  softmax + epilogue  (warp w owns TMEM lanes 32w..32w+31)
+//   warps 4-7  gather              (cp.async 16 B per lane into a 2-stage ring)
+//   warp  8    TMEM allocator + UMMA issuer (one elected lane)
+//
+// Index handling: the CTA first compacts its chunk of the index list to the
+// valid entries (order preserved), so masked indices cost neither bandwidth
+// nor tensor work, a fully masked chunk costs nothing, and out-of-range rows
+// are never addressed. Tiles are 64 compacted rows; the last tile's tail is
+// zero-filled in shared memory and masked in the softmax.
+//
+// Math per 64-row tile (bf16 operands, fp32 accumulation):
+//   GEMM1  S[h, i]  = Q[h, :] . KV[i, :]        M=64 (heads, zero-padded),
+//          N=64 (rows), K=512; A=Q and B=KV both K-major in smem; S in TMEM.
+//   softmax in the log2 domain on S * (sm_scale * log2 e); P -> smem (bf16).
+//   GEMM2  O^T[d, h] += KV^T[d, i] . P^T[i, h]   M=128 (d, four chunks),
+//          N=NH (heads), K=64; A=KV read MN-major from the same smem tile,
+//          B=P K-major; O^T accumulates in TMEM across all tiles.
+// The running max only moves when a head's tile max exceeds it by more than
+// 2^8; then the O^T columns of the moved heads are rescaled in TMEM.
+//
+// Shared-memory operands use the canonical 128-byte-swizzle layout: a tile is
+// stored as 64-element (128 B) column blocks; inside a block, row r sits at
+// r * 128 and its 16-byte chunk c at ((c ^ (r % 8)) * 16). The KV tile serves
+// GEMM1 as a K-major operand and GEMM2 as an MN-major one without re-layout.
+//
+// Every pipeline wait is bounded in wall time; on expiry the CTA raises a
+// device status bit, finishes without further waiting and releases its TMEM.
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+#include <cstdlib>
+#include <mutex>
+
+#include "glm53_sparse_mla.h"
+#include "sm100_ptx.cuh"
+
+namespace glm53 {
+
+constexpr int kDim = 512;           // latent width = head size
+constexpr int kRows = 64;           // KV rows per pipeline tile
+constexpr int kMaxChunk = 2048;     // indices one CTA can hold after compaction
+constexpr int kThreads = 288;       // 9 warps
+constexpr int kProducerWarp0 = 4;   // warps 4-7 gather
+constexpr int kMmaWarp = 8;
+constexpr int kTmemCols = 512;
+constexpr uint32_t kTmemS = 256;    // S double buffer at columns 256 and 320
+constexpr float kRescaleThreshold = 8.0f;   // log2 units: rescale when max grows > 256x
+
+// Shared-memory map (byte offsets from a 1024-aligned base).
+constexpr uint32_t kSmQ = 0;                          // 64 rows x 512 bf16 = 64 KB
+constexpr uint32_t kStageBytes = 65536;               // 64 rows x 512 bf16
+constexpr uint32_t kSmKV = 65536;                     // 2 stages; reused for the fp32 partial
+constexpr uint32_t kPBytes = 8192;                    // NH rows x 128 B, NH <= 64
+constexpr uint32_t kSmP = kSmKV + 2 * kStageBytes;    // 2 P buffers
+constexpr uint32_t kSmIdx = kSmP + 2 * kPBytes;       // int32[kMaxChunk]
+constexpr uint32_t kSmHead = kSmIdx + 4 * kMaxChunk;  // m[64] l[64] alpha[64] f[64]
+constexpr uint32_t kSmBar = kSmHead + 4 * 64 * 4;     // mbarriers
+constexpr uint32_t kSmMisc = kSmBar + 16 * 8;         // tmem base, counts, abort flag
+constexpr uint32_t kSmUsed = kSmMisc + 64;
+constexpr uint32_t kSmemBytes = kSmUsed + 1024;       // + slack to align the base
+
+// mbarrier slots
+enum : int {
+  kBarKvFull = 0,    // [2] producers -> MMA: stage loaded
+  kBarKvEmpty = 2,   // [2] MMA (commit) -> producers: stage consumed by GEMM2
+  kBarSFull = 4,     // [2] MMA (commit) -> softmax: S ready
+  kBarSEmpty = 6,    // [2] softmax -> MMA: S buffer read
+  kBarPFull = 8,     // [2] softmax -> MMA: P written (and O rescaled)
+  kBarODone = 10,    // MMA (commit) -> softmax: a GEMM2 finished
+  kBarDrain = 11,    // MMA (commit) -> MMA: every UMMA finished
+  kNumBars = 12
+};
+
+// misc words
+enum : int { kMiscTmem = 0, kMiscWarpCount = 2, kMiscAbort = 10 };
+
+struct Params {
+  const __nv_bfloat16* q;   // [T, H, 512]
+  const void* kv;           // [R, 512] bf16 or fp8_e4m3
+  const int32_t* idx;       // [T, topk]
+  __nv_bfloat16* out;       // [T, H, 512]
+  float* lse;               // [T, H] or nullptr
+  long long kv_rows;
+  int T, H, topk, splits, chunk;
+  float c;                  // sm_scale * log2(e)
+  float kv_scale;
+  unsigned long long timeout_ns;
+};
+
+__device__ unsigned int g_device_status = 0;
+
+__device__ __forceinline__ uint32_t swz(uint32_t row, uint32_t chunk) {
+  // byte offset of 16-byte chunk `chunk` (0..63) of row `row` in a tile of
+  // 64-element column blocks, each block (rows x 128 B) 8192 B apart
+  return (chunk >> 3) * 8192u + row * 128u + (((chunk & 7u) ^ (row & 7u)) << 4);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&b);
+}
+
+// Two e4m3 values (low byte first) -> two bf16 of value * scale. e4m3 -> f16 is
+// exact, the product is rounded once in fp32 and once to bf16, i.e. the same
+// value as bf16(float(e4m3) * scale).
+__device__ __forceinline__ uint32_t dequant2(uint32_t two, float scale) {
+  const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(two),
+                                                    __NV_E4M3);
+  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+  return pack_bf16x2(f.x * scale, f.y * scale);
+}
+
+__device__ __forceinline__ void dequant16(const uint4 w, float scale, uint4& lo, uint4& hi) {
+  lo.x = dequant2(w.x & 0xFFFFu, scale);
+  lo.y = dequant2(w.x >> 16, scale);
+  lo.z = dequant2(w.y & 0xFFFFu, scale);
+  lo.w = dequant2(w.y >> 16, scale);
+  hi.x = dequant2(w.z & 0xFFFFu, scale);
+  hi.y = dequant2(w.z >> 16, scale);
+  hi.z = dequant2(w.w & 0xFFFFu, scale);
+  hi.w = dequant2(w.w >> 16, scale);
+}
+
+template <int NH, bool kFp8>
+__global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __grid_constant__ Params p) {
+  static_assert(NH == 16 || NH == 32 || NH == 64, "padded head count");
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t sb = (raw + 1023u) & ~1023u;
+  uint8_t* const gb = smem_raw + (sb - raw);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int split = static_cast<int>(blockIdx.x) % p.splits;
+  const int token = static_cast<int>(blockIdx.x) / p.splits;
+
+  float* const m_sm = reinterpret_cast<float*>(gb + kSmHead);
+  float* const l_sm = m_sm + 64;
+  float* const alpha_sm = m_sm + 128;
+  float* const f_sm = m_sm + 192;
+  int32_t* const idx_sm = reinterpret_cast<int32_t*>(gb + kSmIdx);
+  uint32_t* const misc = reinterpret_cast<uint32_t*>(gb + kSmMisc);
+  volatile int* const abort_flag = reinterpret_cast<volatile int*>(misc + kMiscAbort);
+  auto bar = [sb](int i) -> uint32_t { return sb + kSmBar + 8u * static_cast<uint32_t>(i); };
+
+  // ------------------------------------------------------------------ setup
+  if (tid == 0) {
+    mbar_init(bar(kBarKvFull + 0), 128);
+    mbar_init(bar(kBarKvFull + 1), 128);
+    mbar_init(bar(kBarKvEmpty + 0), 1);
+    mbar_init(bar(kBarKvEmpty + 1), 1);
+    mbar_init(bar(kBarSFull + 0), 1);
+    mbar_init(bar(kBarSFull + 1), 1);
+    mbar_init(bar(kBarSEmpty + 0), 128);
+    mbar_init(bar(kBarSEmpty + 1), 128);
+    mbar_init(bar(kBarPFull + 0), 128);
+    mbar_init(bar(kBarPFull + 1), 128);
+    mbar_init(bar(kBarODone), 1);
+    mbar_init(bar(kBarDrain), 1);
+    misc[kMiscAbort] = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(sb + kSmMisc + 4 * kMiscTmem, kTmemCols);
+    tmem_relinquish();
+  }
+
+  // Q (all 64 rows of the M=64 operand; rows >= H are zero) via cp.async.
+  {
+    const __nv_bfloat16* qtok = p.q + static_cast<size_t>(token) * p.H * kDim;
+    for (int u = tid; u < 64 * 64; u += kThreads) {
+      const int h = u >> 6, c = u & 63;
+      const bool ok = h < p.H;
+      cp_async_16(sb + kSmQ + swz(h, c), qtok + (ok ? h : 0) * kDim + c * 8, ok ? 16u : 0u);
+    }
+  }
+
+  // Index compaction, pass 1: warps 0-7 each take a contiguous sub-range of
+  // this CTA's chunk, keep it in registers and count the valid entries.
+  const int k0 = split * p.chunk;
+  const int len = max(0, min(p.chunk, p.topk - k0));
+  const int per_warp = ((len + 255) / 256) * 32;   // multiple of 32, <= 256
+  int32_t vals[8];
+  uint32_t masks[8];
+  if (warp < 8) {
+    const int32_t* irow = p.idx + static_cast<size_t>(token) * p.topk + k0;
+    int cnt = 0;
+    bool bad = false;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int k = warp * per_warp + j * 32 + lane;
+      int32_t v = -1;
+      if (j * 32 < per_warp && k < len) v = irow[k];
+      const bool valid = v >= 0 && static_cast<long long>(v) < p.kv_rows;
+      bad |= (v >= 0) && !valid;
+      vals[j] = v;
+      masks[j] = __ballot_sync(0xFFFFFFFFu, valid);
+      cnt += __popc(masks[j]);
+    }
+    if (lane == 0) misc[kMiscWarpCount + warp] = static_cast<uint32_t>(cnt);
+    if (bad) atomicOr(&g_device_status, static_cast<unsigned>(GLM53_DEV_BAD_INDEX));
+  }
+  cp_async_wait_all();
+  fence_proxy_async_smem();   // Q bytes written by cp.async -> tensor-core reads
+  __syncthreads();
+
+  // pass 2: scatter the valid entries to their compacted positions
+  int n_valid = 0, base = 0;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    const int c = static_cast<int>(misc[kMiscWarpCount + w]);
+    if (w < warp) base += c;
+    n_valid += c;
+  }
+  if (warp < 8) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t m = masks[j];
+      if (m & (1u << lane)) idx_sm[base + __popc(m & ((1u << lane) - 1u))] = vals[j];
+      base += __popc(m);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = misc[kMiscTmem];
+  const int n_tiles = (n_valid + kRows - 1) / kRows;
+
+  // ------------------------------------------------------------------ roles
+  if (warp >= kProducerWarp0 && warp < kMmaWarp) {
+    // ================= gather =================
+    const int pw = warp - kProducerWarp0;
+    for (int t = 0; t < n_tiles; ++t) {
+      const int s = t & 1;
+      if (t >= 2 &&
+          !mbar_wait_bounded(bar(kBarKvEmpty + s), ((t >> 1) - 1) & 1, abort_flag, p.timeout_ns))
+        break;
+      const uint32_t stage = sb + kSmKV + s * kStageBytes;
+      const int rows = min(kRows, n_valid - kRows * t);
+      if constexpr (!kFp8) {
+        const uint8_t* kvb = static_cast<const uint8_t*>(p.kv);
+#pragma unroll 4
+        for (int r = pw; r < kRows; r += 4) {
+          const bool valid = r < rows;
+          const long long row = valid ? idx_sm[kRows * t + r] : 0;
+          const uint8_t* src = kvb + row * (kDim * 2);
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const int c = lane + 32 * hh;
+            cp_async_16(stage + swz(r, c), src + c * 16, valid ? 16u : 0u);
+          }
+        }
+        cp_async_mbar_arrive_noinc(bar(kBarKvFull + s));
+      } else {
+        const uint8_t* kv8 = static_cast<const uint8_t*>(p.kv);
+        uint4 buf[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int r = pw + 4 * j;
+          if (r < rows) {
+            const long long row = idx_sm[kRows * t + r];
+            buf[j] = ldg_nc_v4(kv8 + row * kDim + lane * 16);
+          } else {
+            buf[j] = make_uint4(0u, 0u, 0u, 0u);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int r = pw + 4 * j;
+          uint4 lo, hi;
+          dequant16(buf[j], p.kv_scale, lo, hi);
+          sts_v4(stage + swz(r, 2 * lane), lo);
+          sts_v4(stage + swz(r, 2 * lane + 1), hi);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(bar(kBarKvFull + s));
+      }
+    }
+    cp_async_wait_all();
+    __syncwarp();
+  } else if (warp == kMmaWarp) {
+    // ================= UMMA issue =================
+    if (lane == 0) {
+      constexpr uint32_t kIdesc1 = idesc_bf16_f32(64, 64, false, false);
+      constexpr uint32_t kIdesc2 = idesc_bf16_f32(128, NH, true, false);
+      auto gemm1 = [&](int t) {
+        const uint32_t stage = sb + kSmKV + (t & 1) * kStageBytes;
+        const uint32_t d_tmem = tmem + kTmemS + 64u * (t & 1);
+#pragma unroll
+        for (int kk = 0; kk < kDim / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 8192u + (kk & 3) * 32u;
+          umma_bf16(d_tmem, sdesc_sw128(sb + kSmQ + off, 16, 1024),
+                    sdesc_sw128(stage + off, 16, 1024), kIdesc1, kk > 0 ? 1u : 0u);
+        }
+      };
+      auto gemm2 = [&](int t) {
+        const uint32_t stage = sb + kSmKV + (t & 1) * kStageBytes;
+        const uint32_t pbuf = sb + kSmP + (t & 1) * kPBytes;
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+#pragma unroll
+          for (int kk = 0; kk < kRows / 16; ++kk) {
+            umma_bf16(tmem + static_cast<uint32_t>(m * NH),
+                      sdesc_sw128(stage + m * 16384u + kk * 2048u, 8192, 1024),
+                      sdesc_sw128(pbuf + kk * 32u, 16, 1024), kIdesc2,
+                      (t > 0 || kk > 0) ? 1u : 0u);
+          }
+        }
+      };
+      bool ok = true;
+      for (int t = 0; t < n_tiles && ok; ++t) {
+        const int s = t & 1;
+        ok = mbar_wait_bounded(bar(kBarKvFull + s), (t >> 1) & 1, abort_flag, p.timeout_ns);
+        if (!ok) break;
+        fence_proxy_async_smem();
+        if (t >= 2) {
+          ok = mbar_wait_bounded(bar(kBarSEmpty + s), ((t >> 1) - 1) & 1, abort_flag,
+                                 p.timeout_ns);
+          if (!ok) break;
+        }
+        tc_fence_after();
+        gemm1(t);
+        umma_commit(bar(kBarSFull + s));
+        if (t >= 1) {
+          const int u = t - 1;
+          ok = mbar_wait_bounded(bar(kBarPFull + (u & 1)), (u >> 1) & 1, abort_flag, p.timeout_ns);
+          if (!ok) break;
+          tc_fence_after();
+          gemm2(u);
+          umma_commit(bar(kBarKvEmpty + (u & 1)));
+          umma_commit(bar(kBarODone));
+        }
+      }
+      if (ok && n_tiles > 0) {
+        const int u = n_tiles - 1;
+        if (mbar_wait_bounded(bar(kBarPFull + (u & 1)), (u >> 1) & 1, abort_flag, p.timeout_ns)) {
+          tc_fence_after();
+          gemm2(u);
+          umma_commit(bar(kBarKvEmpty + (u & 1)));
+          umma_commit(bar(kBarODone));
+        }
+      }
+      // Drain: never release TMEM while a UMMA may still write it.
+      umma_commit(bar(kBarDrain));
+      int no_abort = 0;
+      mbar_wait_bounded(bar(kBarDrain), 0, &no_abort, p.timeout_ns);
+    }
+    __syncwarp();
+  } else {
+    // ================= softmax (warps 0-3) =================
+    const int q4 = warp;                       // TMEM lane quadrant
+    const int h = 16 * q4 + (lane & 15);       // head owned (M=64 layout)
+    const int half = lane >> 4;                // which 32 of the 64 tile rows
+    const bool has_head = (16 * q4) < NH;      // warp-uniform
+    const uint32_t lane_base = static_cast<uint32_t>(32 * q4) << 16;
+    float m_used = -INFINITY;   // running max, log2 units (score * c)
+    float l_part = 0.f;         // this thread's share of the running sum
+
+    for (int t = 0; t < n_tiles; ++t) {
+      const int b = t & 1;
+      // A failed wait leaves the loop running on garbage with every barrier
+      // still taken, so no thread of the group can strand the others.
+      mbar_wait_bounded(bar(kBarSFull + b), (t >> 1) & 1, abort_flag, p.timeout_ns);
+      tc_fence_after();
+      float v[32];
+      if (has_head) {
+        tmem_ld_16x32bx2_x32(tmem + lane_base + kTmemS + 64u * b, v);
+        tmem_wait_ld();
+      }
+      tc_fence_before();
+      mbar_arrive(bar(kBarSEmpty + b));
+
+      const int rows = min(kRows, n_valid - kRows * t);
+      float mx = -INFINITY;
+      if (has_head) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const bool valid = 32 * half + j < rows;
+          v[j] = valid ? v[j] * p.c : -INFINITY;
+          mx = fmaxf(mx, v[j]);
+        }
+      }
+      mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 16));
+      const bool need = has_head && (mx > m_used + kRescaleThreshold);
+      const float new_m = need ? mx : m_used;
+      const float alpha = need ? exp2f(m_used - new_m) : 1.f;
+
+      __syncwarp();
+      if (named_bar_or(1, 128, need && t > 0)) {
+        if (has_head && half == 0) alpha_sm[h] = alpha;
+        named_bar_sync(1, 128);
+        // O^T must hold GEMM2(t-1) in full before it is rescaled.
+        mbar_wait_bounded(bar(kBarODone), (t - 1) & 1, abort_flag, p.timeout_ns);
+        tc_fence_after();
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          if constexpr (NH == 16) {
+            float o[16];
+            const uint32_t ta = tmem + lane_base + static_cast<uint32_t>(m * NH);
+            tmem_ld_32x32b_x16(ta, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) o[j] *= alpha_sm[j];
+            tmem_st_32x32b_x16(ta, o);
+          } else {
+#pragma unroll
+            for (int cc = 0; cc < NH / 32; ++cc) {
+              float o[32];
+              const uint32_t ta = tmem + lane_base + static_cast<uint32_t>(m * NH + 32 * cc);
+              tmem_ld_32x32b_x32(ta, o);
+              tmem_wait_ld();
+#pragma unroll
+              for (int j = 0; j < 32; ++j) o[j] *= alpha_sm[32 * cc + j];
+              tmem_st_32x32b_x32(ta, o);
+            }
+          }
+        }
+        tmem_wait_st();
+        // alpha_sm is rewritten only after the next p_full wait of the MMA
+        // warp, which this group's arrive below gates; nothing else to order.
+      }
+      l_part *= alpha;
+      m_used = new_m;
+
+      if (has_head) {
+        uint32_t packed[16];
+        float ps = 0.f;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float p0 = exp2f(v[2 * j] - m_used);
+          const float p1 = exp2f(v[2 * j + 1] - m_used);
+          ps += p0 + p1;
+          packed[j] = pack_bf16x2(p0, p1);
+        }
+        l_part += ps;
+        const uint32_t prow = sb + kSmP + b * kPBytes + static_cast<uint32_t>(h) * 128u;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint32_t c = static_cast<uint32_t>(4 * half + k);
+          sts_v4(prow + ((c ^ (static_cast<uint32_t>(h) & 7u)) << 4),
+                 make_uint4(packed[4 * k], packed[4 * k + 1], packed[4 * k + 2], packed[4 * k + 3]));
+        }
+        fence_proxy_async_smem();
+      }
+      tc_fence_before();
+      mbar_arrive(bar(kBarPFull + b));
+    }
+
+    // publish this CTA's per-head max and sum for the cluster merge
+    __syncwarp();
+    const float l_tot = l_part + __shfl_xor_sync(0xFFFFFFFFu, l_part, 16);
+    if (has_head && half == 0) {
+      m_sm[h] = n_tiles > 0 ? m_used : -INFINITY;
+      l_sm[h] = n_tiles > 0 ? l_tot : 0.f;
+    }
+  }
+
+  // ------------------------------------------------------------------ merge
+  const int nranks = p.splits;
+  cluster_sync_all();   // (A) every CTA's m/l visible cluster-wide
+
+  if (warp < 4) {
+    if (tid < NH) {
+      const int hh = tid;
+      const uint32_t m_addr = sb + kSmHead + 4u * hh;
+      const uint32_t l_addr = m_addr + 256u;
+      float M = -INFINITY;
+      for (int r = 0; r < nranks; ++r) {
+        const float lr = ld_dsmem_f32(mapa_shared(l_addr, r));
+        if (lr > 0.f) M = fmaxf(M, ld_dsmem_f32(mapa_shared(m_addr, r)));
+      }
+      float L = 0.f;
+      for (int r = 0; r < nranks; ++r) {
+        const float lr = ld_dsmem_f32(mapa_shared(l_addr, r));
+        if (lr > 0.f) L += lr * exp2f(ld_dsmem_f32(mapa_shared(m_addr, r)) - M);
+      }
+      const float l_own = l_sm[hh];
+      f_sm[hh] = (L > 0.f && l_own > 0.f) ? exp2f(m_sm[hh] - M) / L : 0.f;
+      if (split == 0 && p.lse != nullptr && hh < p.H)
+        p.lse[static_cast<size_t>(token) * p.H + hh] = L > 0.f ? log2f(L) + M : -INFINITY;
+    }
+    named_bar_sync(1, 128);
+
+    // scaled partial O^T -> fp32 [NH][512] in the (now idle) KV stage region
+    if (n_tiles > 0)
+      mbar_wait_bounded(bar(kBarODone), (n_tiles - 1) & 1, abort_flag, p.timeout_ns);
+    tc_fence_after();
+    float* const part = reinterpret_cast<float*>(gb + kSmKV);
+    const uint32_t lane_base = static_cast<uint32_t>(32 * warp) << 16;
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const int d = 128 * m + 32 * warp + lane;
+      if constexpr (NH == 16) {
+        float o[16];
+        tmem_ld_32x32b_x16(tmem + lane_base + static_cast<uint32_t>(m * NH), o);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) part[j * kDim + d] = n_tiles > 0 ? o[j] * f_sm[j] : 0.f;
+      } else {
+#pragma unroll
+        for (int cc = 0; cc < NH / 32; ++cc) {
+          float o[32];
+          tmem_ld_32x32b_x32(tmem + lane_base + static_cast<uint32_t>(m * NH + 32 * cc), o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            part[(32 * cc + j) * kDim + d] = n_tiles > 0 ? o[j] * f_sm[32 * cc + j] : 0.f;
+        }
+      }
+    }
+    tc_fence_before();
+  }
+  cluster_sync_all();   // (B) every CTA's scaled partial visible cluster-wide
+
+  // Each CTA of the cluster sums one d-slice over all ranks and writes bf16.
+  {
+    const int dspan = kDim / nranks;
+    const int units_per_head = dspan / 8;
+    const int units = p.H * units_per_head;
+    for (int u = tid; u < units; u += kThreads) {
+      const int hh = u / units_per_head;
+      const int d = split * dspan + (u % units_per_head) * 8;
+      const uint32_t off = sb + kSmKV + static_cast<uint32_t>(hh * kDim + d) * 4u;
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int r = 0; r < nranks; ++r) {
+        const uint32_t a = mapa_shared(off, r);
+        const float4 x = ld_dsmem_v4(a);
+        const float4 y = ld_dsmem_v4(a + 16);
+        acc[0] += x.x; acc[1] += x.y; acc[2] += x.z; acc[3] += x.w;
+        acc[4] += y.x; acc[5] += y.y; acc[6] += y.z; acc[7] += y.w;
+      }
+      stg_v4(p.out + (static_cast<size_t>(token) * p.H + hh) * kDim + d,
+             make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
+                        pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7])));
+    }
+  }
+  cluster_sync_all();   // (C) no CTA leaves while a peer still reads its smem
+
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+  if (tid == 0 && *abort_flag) atomicOr(&g_device_status, static_cast<unsigned>(GLM53_DEV_TIMEOUT));
+}
+
+// ---------------------------------------------------------------------------
+// gather-only probe: same access pattern as the attention gather, no math
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+__global__ void __launch_bounds__(256, 1) gather_roof_kernel(const uint8_t* __restrict__ kv,
+                                                             const int32_t* __restrict__ idx,
+                                                             int topk, long long kv_rows,
+                                                             uint32_t* sink) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  const uint32_t sb = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int32_t* irow = idx + static_cast<size_t>(blockIdx.x) * topk;
+  const int ntiles = (topk + kRows - 1) / kRows;
+  for (int t = 0; t < ntiles; ++t) {
+    const uint32_t stage = sb + (t & 1) * kStageBytes;
+    for (int r = warp; r < kRows; r += 8) {
+      const int k = kRows * t + r;
+      const int32_t v = k < topk ? irow[k] : -1;
+      const bool valid = v >= 0 && v < kv_rows;
+      const uint8_t* src = kv + (valid ? static_cast<long long>(v) : 0) * (kDim * 2);
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int c = lane + 32 * hh;
+        cp_async_16(stage + swz(r, c), src + c * 16, valid ? 16u : 0u);
+      }
+    }
+    cp_async_commit();
+    cp_async_wait_1();
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  uint32_t x;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(x) : "r"(sb + threadIdx.x * 4));
+  if (x == 0x9E3779B9u && sink != nullptr) sink[0] = x;   // keep the copies observable
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+constexpr int kMaxDevices = 64;
+std::mutex g_mutex;
+bool g_prepared[kMaxDevices] = {};
+int g_sm_count[kMaxDevices] = {};
+int g_cc_major[kMaxDevices] = {};
+unsigned long long g_timeout_ns = 0;
+
+template <int NH, bool FP8>
+cudaError_t launch_fwd(const Params& p, int splits, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(p.T) * static_cast<unsigned>(splits), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = splits > 1 ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, sparse_mla_fwd_kernel<NH, FP8>, p);
+}
+
+template <int NH, bool FP8>
+cudaError_t set_smem_attr() {
+  return cudaFuncSetAttribute(sparse_mla_fwd_kernel<NH, FP8>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(kSmemBytes));
+}
+
+int prepare_current_device(int* dev_out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return GLM53_ERR_CUDA;
+  if (dev < 0 || dev >= kMaxDevices) return GLM53_ERR_CUDA;
+  if (dev_out) *dev_out = dev;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if (g_prepared[dev]) return GLM53_OK;
+  if (g_timeout_ns == 0) {
+    const char* env = std::getenv("GLM53_WAIT_TIMEOUT_MS");
+    const long long ms = env ? std::atoll(env) : 0;
+    g_timeout_ns = static_cast<unsigned long long>(ms > 0 ? ms : 1000) * 1000000ull;
+  }
+  int major = 0, sms = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return GLM53_ERR_CUDA;
+  g_cc_major[dev] = major;
+  g_sm_count[dev] = sms;
+  if (major != 10) return GLM53_ERR_DEVICE;
+  cudaError_t e = cudaSuccess;
+  if (e == cudaSuccess) e = set_smem_attr<16, false>();
+  if (e == cudaSuccess) e = set_smem_attr<32, false>();
+  if (e == cudaSuccess) e = set_smem_attr<64, false>();
+  if (e == cudaSuccess) e = set_smem_attr<16, true>();
+  if (e == cudaSuccess) e = set_smem_attr<32, true>();
+  if (e == cudaSuccess) e = set_smem_attr<64, true>();
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(gather_roof_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(2 * kStageBytes + 1024));
+  if (e != cudaSuccess) return GLM53_ERR_CUDA;
+  g_prepared[dev] = true;
+  return GLM53_OK;
+}
+
+bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+}  // namespace glm53
+
+using namespace glm53;
+
+extern "C" int glm53_sparse_mla_check(int64_t T, int64_t H, int64_t head_dim, int64_t kv_rows,
+                                      int64_t kv_width, int64_t topk, int kv_dtype, int splits) {
+  if (T < 0 || kv_rows < 0 || topk < 0) return GLM53_ERR_RANK;
+  if (head_dim != kDim || kv_width != kDim) return GLM53_ERR_HEAD_DIM;
+  if (kv_dtype != GLM53_KV_BF16 && kv_dtype != GLM53_KV_FP8_E4M3) return GLM53_ERR_DTYPE;
+  if (H != 8 && H != 16 && H != 32 && H != 64) return GLM53_ERR_HEADS;
+  if (topk % 32 != 0 || topk > 8 * kMaxChunk) return GLM53_ERR_TOPK;
+  if (splits != 0 && splits != 1 && splits != 2 && splits != 4 && splits != 8)
+    return GLM53_ERR_SPLITS;
+  if (splits != 0 && (topk + splits - 1) / splits > kMaxChunk) return GLM53_ERR_TOPK;
+  if (T > (int64_t{1} << 28) || kv_rows > (int64_t{1} << 31)) return GLM53_ERR_RANK;
+  return GLM53_OK;
+}
+
+extern "C" int glm53_sparse_mla_auto_splits(int64_t T, int64_t topk, int sm_count) {
+  if (T <= 0) return 1;
+  int s = 1;
+  // widen while the grid still fits in one wave and each CTA keeps >= 4 tiles
+  while (s < 8 && T * (2 * s) <= sm_count && topk / (2 * s) >= 4 * kRows) s *= 2;
+  while ((topk + s - 1) / s > kMaxChunk && s < 8) s *= 2;
+  return s;
+}
+
+extern "C" int glm53_sparse_mla_prepare(void) { return prepare_current_device(nullptr); }
+
+extern "C" int glm53_sparse_mla_fwd(const void* q, const void* kv, const int32_t* indices,
+                                    void* out, float* lse, int64_t T, int64_t H, int64_t head_dim,
+                                    int64_t kv_rows, int64_t kv_width, int64_t topk, int kv_dtype,
+                                    float sm_scale, float kv_scale, int splits, void* stream) {
+  int rc = glm53_sparse_mla_check(T, H, head_dim, kv_rows, kv_width, topk, kv_dtype, splits);
+  if (rc != GLM53_OK) return rc;
+  if (T == 0) return GLM53_OK;
+  if (!aligned16(q) || !aligned16(kv) || !aligned16(indices) || !aligned16(out) ||
+      q == nullptr || kv == nullptr || indices == nullptr || out == nullptr)
+    return GLM53_ERR_ALIGN;
+  if (lse != nullptr && (reinterpret_cast<uintptr_t>(lse) & 3u) != 0) return GLM53_ERR_ALIGN;
+  int dev = 0;
+  rc = prepare_current_device(&dev);
+  if (rc != GLM53_OK) return rc;
+  const int s = splits != 0 ? splits : glm53_sparse_mla_auto_splits(T, topk, g_sm_count[dev]);
+  if ((topk + s - 1) / s > kMaxChunk) return GLM53_ERR_TOPK;
+
+  Params p;
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.kv = kv;
+  p.idx = indices;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.lse = lse;
+  p.kv_rows = kv_rows;
+  p.T = static_cast<int>(T);
+  p.H = static_cast<int>(H);
+  p.topk = static_cast<int>(topk);
+  p.splits = s;
+  p.chunk = static_cast<int>((topk + s - 1) / s);
+  p.c = sm_scale * 1.4426950408889634f;
+  p.kv_scale = kv_dtype == GLM53_KV_BF16 ? 1.0f : kv_scale;
+  p.timeout_ns = g_timeout_ns;
+
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool fp8 = kv_dtype == GLM53_KV_FP8_E4M3;
+  cudaError_t e;
+  if (H <= 16)
+    e = fp8 ? launch_fwd<16, true>(p, s, st) : launch_fwd<16, false>(p, s, st);
+  else if (H == 32)
+    e = fp8 ? launch_fwd<32, true>(p, s, st) : launch_fwd<32, false>(p, s, st);
+  else
+    e = fp8 ? launch_fwd<64, true>(p, s, st) : launch_fwd<64, false>(p, s, st);
+  return e == cudaSuccess ? GLM53_OK : GLM53_ERR_CUDA;
+}
+
+extern "C" int glm53_sparse_mla_device_status(uint32_t* status, int clear) {
+  unsigned int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_device_status, sizeof(v)) != cudaSuccess) return GLM53_ERR_CUDA;
+  if (status) *status = v;
+  if (clear) {
+    const unsigned int zero = 0;
+    if (cudaMemcpyToSymbol(g_device_status, &zero, sizeof(zero)) != cudaSuccess)
+      return GLM53_ERR_CUDA;
+  }
+  return GLM53_OK;
+}
+
+extern "C" int glm53_gather_roof(const void* kv, const int32_t* indices, int64_t T, int64_t topk,
+                                 int64_t kv_rows, void* sink, void* stream) {
+  if (T < 0 || topk < 0 || kv_rows < 0) return GLM53_ERR_RANK;
+  if (T == 0 || topk == 0) return GLM53_OK;
+  if (kv == nullptr || indices == nullptr || !aligned16(kv)) return GLM53_ERR_ALIGN;
+  const int rc = prepare_current_device(nullptr);
+  if (rc != GLM53_OK) return rc;
+  gather_roof_kernel<<<static_cast<unsigned>(T), 256, 2 * kStageBytes + 1024,
+                       static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(kv), indices, static_cast<int>(topk), kv_rows,
+      static_cast<uint32_t*>(sink));
+  return cudaGetLastError() == cudaSuccess ? GLM53_OK : GLM53_ERR_CUDA;
+}
+
+extern "C" const char* glm53_sparse_mla_strerror(int code) {
+  switch (code) {
+    case GLM53_OK: return "ok";
+    case GLM53_ERR_RANK: return "expected q [T, H, 512], kv [R, 512], indices [T, topk], out shaped like q";
+    case GLM53_ERR_HEAD_DIM: return "expected kv_lora_rank 512 with qk_rope_head_dim 0 (NoPE)";
+    case GLM53_ERR_HEADS: return "unsupported heads-per-rank; built for 8, 16, 32 or 64 (TP=8/4/2/1 on a 64-head model)";
+    case GLM53_ERR_TOPK: return "topk must be a multiple of 32 and at most 16384";
+    case GLM53_ERR_DTYPE: return "kv must be bfloat16 or float8_e4m3fn";
+    case GLM53_ERR_ALIGN: return "a tensor pointer is null or not 16-byte aligned";
+    case GLM53_ERR_SPLITS: return "splits must be 0 (auto), 1, 2, 4 or 8";
+    case GLM53_ERR_CUDA: return "CUDA runtime error while launching the sparse-MLA kernel";
+    case GLM53_ERR_DEVICE: return "the current device is not an sm_100 (B200-class) GPU";
+    default: return "unknown glm53_sparse_mla status";
+  }
+}

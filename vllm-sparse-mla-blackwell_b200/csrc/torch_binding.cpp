@@ -1,0 +1,89 @@
+// PyTorch operator binding for the sparse-MLA C ABI.
+//
+// Registers `torch.ops.glm53_sparse_mla.sparse_fwd` with the exact schema of
+// the reference extension (csrc/sparse_mla.cu:500-505) so that existing
+// callers (the vLLM backend, tests, benches) bind unchanged, plus
+// `sparse_fwd_lse`, which also returns the per-(token, head) log2-space LSE.
+// Argument checks mirror the reference host op (csrc/sparse_mla.cu:455-498):
+// same conditions, same order (T == 0 returns before the dtype / head-count
+// dispatch), raised as RuntimeError through TORCH_CHECK. The launch itself goes
+// through glm53_sparse_mla_fwd on the caller's current CUDA stream.
+
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+#include <torch/all.h>
+
+#include "glm53_sparse_mla.h"
+
+namespace {
+
+constexpr int64_t kDim = 512;
+
+void run_sparse_fwd(const torch::Tensor& q, const torch::Tensor& kv, const torch::Tensor& indices,
+                    double sm_scale, double kv_scale, torch::Tensor& out, float* lse) {
+  TORCH_CHECK(q.is_cuda() && kv.is_cuda() && indices.is_cuda() && out.is_cuda(),
+              "glm53_sparse_mla: q, kv, indices and out must be CUDA tensors");
+  TORCH_CHECK(q.dim() == 3 && kv.dim() == 2 && indices.dim() == 2,
+              "glm53_sparse_mla: expected q [T, H, 512], kv [R, 512], indices [T, topk]");
+  TORCH_CHECK(q.scalar_type() == torch::kBFloat16, "glm53_sparse_mla: q must be bfloat16");
+  TORCH_CHECK(indices.scalar_type() == torch::kInt, "glm53_sparse_mla: indices must be int32");
+  TORCH_CHECK(q.is_contiguous() && kv.is_contiguous() && indices.is_contiguous(),
+              "glm53_sparse_mla: q, kv and indices must be contiguous");
+  TORCH_CHECK(q.size(2) == kDim && kv.size(1) == kDim, "expected kv_lora_rank ", kDim,
+              " with qk_rope_head_dim 0 (NoPE)");
+  const int64_t T = q.size(0);
+  const int64_t topk = indices.size(1);
+  TORCH_CHECK(topk % 32 == 0, "glm53_sparse_mla: topk must be a multiple of 32, got ", topk);
+  TORCH_CHECK(indices.size(0) == T && out.sizes() == q.sizes(),
+              "glm53_sparse_mla: indices must have T rows and out the shape of q");
+  TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.is_contiguous(),
+              "glm53_sparse_mla: out must be a contiguous bfloat16 tensor");
+  TORCH_CHECK(kv.get_device() == q.get_device() && indices.get_device() == q.get_device() &&
+                  out.get_device() == q.get_device(),
+              "glm53_sparse_mla: all tensors must be on the same device");
+
+  if (T == 0) return;
+
+  int kv_dtype = -1;
+  if (kv.scalar_type() == torch::kBFloat16) kv_dtype = GLM53_KV_BF16;
+  else if (kv.scalar_type() == torch::kFloat8_e4m3fn) kv_dtype = GLM53_KV_FP8_E4M3;
+  TORCH_CHECK(kv_dtype >= 0, "kv must be bfloat16 or float8_e4m3fn, got ", kv.scalar_type());
+  const int64_t H = q.size(1);
+  TORCH_CHECK(H == 8 || H == 16 || H == 32 || H == 64, "unsupported heads-per-rank ", H,
+              "; built for 8, 16, 32 or 64 (TP=8/4/2/1 on a 64-head model)");
+
+  const c10::cuda::CUDAGuard guard(q.device());
+  cudaStream_t stream = c10::cuda::getCurrentCUDAStream(q.get_device()).stream();
+  const int rc = glm53_sparse_mla_fwd(q.data_ptr(), kv.data_ptr(), indices.data_ptr<int32_t>(),
+                                      out.data_ptr(), lse, T, H, q.size(2), kv.size(0),
+                                      kv.size(1), topk, kv_dtype, static_cast<float>(sm_scale),
+                                      static_cast<float>(kv_scale), /*splits=*/0,
+                                      static_cast<void*>(stream));
+  TORCH_CHECK(rc == GLM53_OK, "glm53_sparse_mla: ", glm53_sparse_mla_strerror(rc));
+}
+
+}  // namespace
+
+void sparse_fwd(torch::Tensor q, torch::Tensor kv, torch::Tensor indices, double sm_scale,
+                double kv_scale, torch::Tensor out) {
+  run_sparse_fwd(q, kv, indices, sm_scale, kv_scale, out, nullptr);
+}
+
+void sparse_fwd_lse(torch::Tensor q, torch::Tensor kv, torch::Tensor indices, double sm_scale,
+                    double kv_scale, torch::Tensor out, torch::Tensor lse) {
+  TORCH_CHECK(lse.is_cuda() && lse.scalar_type() == torch::kFloat && lse.is_contiguous() &&
+                  lse.dim() == 2 && q.dim() == 3 && lse.size(0) == q.size(0) &&
+                  lse.size(1) == q.size(1) && lse.get_device() == q.get_device(),
+              "glm53_sparse_mla: lse must be a contiguous float32 CUDA tensor of shape [T, H]");
+  run_sparse_fwd(q, kv, indices, sm_scale, kv_scale, out, lse.data_ptr<float>());
+}
+
+TORCH_LIBRARY(glm53_sparse_mla, m) {
+  m.def("sparse_fwd(Tensor q, Tensor kv, Tensor indices, float sm_scale, float kv_scale, Tensor(a!) out) -> ()");
+  m.def("sparse_fwd_lse(Tensor q, Tensor kv, Tensor indices, float sm_scale, float kv_scale, Tensor(a!) out, Tensor(b!) lse) -> ()");
+}
+
+TORCH_LIBRARY_IMPL(glm53_sparse_mla, CUDA, m) {
+  m.impl("sparse_fwd", &sparse_fwd);
+  m.impl("sparse_fwd_lse", &sparse_fwd_lse);
+}

@@ -1,0 +1,122 @@
+"""Sparse MLA (NoPE) attention for B200 (sm_100a).
+
+Exposes ``torch.ops.glm53_sparse_mla.sparse_fwd`` with the schema of the
+reference extension, so the vLLM backend in :mod:`glm53_sparse_mla.backend`
+and any other caller bind unchanged, plus ``sparse_fwd_lse`` which also returns
+the log2-space log-sum-exp. The op is a thin binding over the C ABI declared in
+``include/glm53_sparse_mla.h`` (``libglm53_sparse_mla.so``); the kernel is a
+hand-written tcgen05/TMEM kernel for sm_100a. There is no CPU or fallback path:
+without the compiled extension the import fails.
+
+Mirrors the reference facade (glm53_sparse_mla/__init__.py:14-85): same
+constants, same ``sparse_fwd`` signature and return value, same fake kernel
+for ``torch.compile``.
+"""
+
+from __future__ import annotations
+
+import os
+
+import torch
+
+__all__ = [
+    "sparse_fwd",
+    "sparse_fwd_with_lse",
+    "HEADS_PER_RANK",
+    "SUPPORTED_HEADS_PER_RANK",
+    "KV_LORA_RANK",
+    "library_path",
+]
+
+# A 64-head model fits on one B200: TP=1 is the default deployment.
+HEADS_PER_RANK = 64
+# 8 / 16 / 32 / 64 heads per rank, i.e. TP=8 / 4 / 2 / 1 on a 64-head model.
+SUPPORTED_HEADS_PER_RANK = (8, 16, 32, 64)
+KV_LORA_RANK = 512  # head_size, since qk_rope_head_dim == 0 (NoPE)
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def library_path() -> str:
+    """Path of the C-ABI shared library (libglm53_sparse_mla.so)."""
+    return os.path.join(_HERE, "libglm53_sparse_mla.so")
+
+
+def _load() -> None:
+    """Register the CUDA ops.
+
+    The op library is TORCH_LIBRARY-only (no PyInit), so it is loaded with
+    ``torch.ops.load_library``. When it is missing but the sources are present
+    (a development checkout) it is built in place first; a deployed package
+    without its compiled extension raises ImportError instead.
+    """
+    if hasattr(torch.ops, "glm53_sparse_mla") and hasattr(
+        torch.ops.glm53_sparse_mla, "sparse_fwd"
+    ):
+        return
+    op_lib = os.path.join(_HERE, "_C.so")
+    if not (os.path.exists(op_lib) and os.path.exists(library_path())):
+        if not os.path.exists(os.path.join(os.path.dirname(_HERE), "csrc")):
+            raise ImportError(
+                "glm53_sparse_mla: no compiled _C.so / libglm53_sparse_mla.so next to "
+                "the package and no csrc/ to build from. The build did not ship its "
+                "extension."
+            )
+        from .build import build
+
+        build()
+    torch.ops.load_library(op_lib)
+
+
+_load()
+
+
+def sparse_fwd(q, kv, indices, sm_scale, kv_scale=1.0, out=None):
+    """Gathered sparse MLA over the top-k indices.
+
+    q       [T, H, 512]  bfloat16, H in SUPPORTED_HEADS_PER_RANK
+    kv      [R, 512]     bfloat16 or float8_e4m3fn; a flat row view of the paged
+                         cache serving as both K and V (absorbed MLA). kv_scale
+                         is vLLM's per-tensor cache scale (ignored for bf16).
+    indices [T, topk]    int32 physical row ids, -1 is the mask sentinel
+    returns [T, H, 512]  bfloat16 (``out`` if given, written in place)
+
+    Causality is not applied here; the indexer owns it. A token whose indices
+    are all masked returns exactly zero (never NaN).
+    """
+    if out is None:
+        out = torch.empty_like(q)
+    torch.ops.glm53_sparse_mla.sparse_fwd(q, kv, indices, float(sm_scale), float(kv_scale), out)
+    return out
+
+
+def sparse_fwd_with_lse(q, kv, indices, sm_scale, kv_scale=1.0, out=None, lse=None):
+    """As :func:`sparse_fwd`, also returning ``lse [T, H]`` float32.
+
+    ``lse = log2(sum_i exp(sm_scale * q . kv_i))`` over the valid indices, i.e.
+    the natural-log LSE times log2(e); -inf for a fully masked (token, head).
+    """
+    if out is None:
+        out = torch.empty_like(q)
+    if lse is None:
+        lse = torch.empty(q.shape[0], q.shape[1], dtype=torch.float32, device=q.device)
+    torch.ops.glm53_sparse_mla.sparse_fwd_lse(
+        q, kv, indices, float(sm_scale), float(kv_scale), out, lse
+    )
+    return out, lse
+
+
+# Shape-only meta kernels so torch.compile can trace through the ops.
+@torch.library.register_fake("glm53_sparse_mla::sparse_fwd")
+def _sparse_fwd_fake(q, kv, indices, sm_scale, kv_scale, out):
+    torch._check(q.dim() == 3 and kv.dim() == 2 and indices.dim() == 2)
+    torch._check(out.shape == q.shape)
+    return None
+
+
+@torch.library.register_fake("glm53_sparse_mla::sparse_fwd_lse")
+def _sparse_fwd_lse_fake(q, kv, indices, sm_scale, kv_scale, out, lse):
+    torch._check(q.dim() == 3 and kv.dim() == 2 and indices.dim() == 2)
+    torch._check(out.shape == q.shape)
+    torch._check(lse.dim() == 2 and lse.shape[0] == q.shape[0] and lse.shape[1] == q.shape[1])
+    return None
