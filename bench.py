@@ -1,0 +1,498 @@
+#!/usr/bin/env python
+"""Benchmark: sparse-MLA query-tokens/s at 64 heads, top-k 2048 (BASELINE C2).
+
+One step = one launch of the sparse-MLA op over one decode batch: 32 query
+tokens x 64 heads, top-k 2048 over a 131072-slot paged bf16 KV pool (block 64,
+random block tables, context 8192). Inputs are synthetic and seeded
+(glm53_sparse_mla.workloads.config_c2); the reference measures on no public
+dataset.
+
+Device number (`value`): K steps captured in one CUDA graph and replayed,
+timed with CUDA events on the launching stream between a barrier and a device
+synchronisation on both sides; max over ranks. Steps rotate over --sets
+independent input sets (own KV pool, q, indices), whose pools together are
+several times the 126 MB L2, so each step's gather is served from HBM.
+
+End-to-end number (`e2e`): the same metric through the public Python API
+(glm53_sparse_mla.sparse_fwd -> torch op -> C ABI) with host buffers: every
+step copies q and indices from pinned host memory, runs the op and copies the
+output back. The KV pool is resident device state (the paged cache).
+
+`roofline`: algorithmic bytes per launch (gathered KV rows per valid index,
+q, out, indices) / average launch time, against the measured HBM copy
+bandwidth in MEASURED_PEAKS.json; `traffic` is DRAM bytes per launch from the
+committed ncu capture summary (profiles/), or null.
+
+`cpu_baseline`: the CPU oracle (numpy fp32 restatement of the reference's
+tests/reference.py) timed on this host's cores over a bounded sample of the
+same workload, rank 0 only.
+
+Multi-GPU (torchrun, one process per GPU): --shard tokens (default) gives
+every rank its own decode batch with all 64 heads (data-parallel attention,
+weak scaling, no collective on the data path); --shard heads splits the 64
+heads of one batch across ranks (tensor-parallel heads, strong scaling), with
+--allgather adding the NCCL all-gather of the output shards.
+
+--impl reference times the reference's CPU implementation of the path (the
+oracle port) on the host cores instead, on rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "vllm-sparse-mla-blackwell_b200"))
+sys.path.insert(0, REPO)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "sparse-MLA query-tokens/s @64 heads, topk=2048 (C2 decode, bf16 KV)"
+UNIT = "query-tokens/s"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5"], default="c2")
+    ap.add_argument("--heads", type=int, default=0, help="heads per launch (0 = workload's)")
+    ap.add_argument("--kv", choices=["bf16", "fp8"], default="bf16", help="C5 KV dtype")
+    ap.add_argument("--sets", type=int, default=8, help="rotating input sets")
+    ap.add_argument("--splits", type=int, default=0, help="force a split count (0 = auto)")
+    ap.add_argument("--shard", choices=["tokens", "heads"], default="tokens")
+    ap.add_argument("--allgather", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# process group
+# ---------------------------------------------------------------------------
+class Dist:
+    def __init__(self, want: int):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        if want != self.world and not (want == 1 and self.world == 1):
+            if self.world == 1 and want > 1:
+                raise SystemExit(f"--gpus {want} needs torchrun with {want} processes")
+        self.pg = None
+
+    def init(self, backend: str):
+        if self.world > 1:
+            import datetime
+            torch.distributed.init_process_group(
+                backend, timeout=datetime.timedelta(seconds=180),
+                device_id=torch.device("cuda", self.local) if backend == "nccl" else None)
+            self.pg = True
+
+    def barrier(self):
+        if self.pg:
+            torch.distributed.barrier()
+
+    def max(self, x: float, device) -> float:
+        if not self.pg:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            torch.distributed.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# workloads
+# ---------------------------------------------------------------------------
+def make_workload(args, W, seed: int, device, heads: int, head_offset: int = 0):
+    if args.workload == "c2":
+        w = W.config_c2(device=device, seed=seed, heads=64)
+    elif args.workload == "c3":
+        w = W.config_c3(device=device, seed=seed)
+    elif args.workload == "c4":
+        w = W.config_c4(device=device, seed=seed)
+    else:
+        w = W.config_c5(device=device, seed=seed, heads=64, kv_dtype=args.kv)
+    if heads and heads != w.H:
+        w.q = w.q[:, head_offset:head_offset + heads].contiguous()
+    return w
+
+
+def workload_desc(args, w, heads_total: int) -> dict:
+    d = {"c2": "C2 decode bf16: 32 seqs x 1 token, 64 heads, topk 2048, pool 131072 slots",
+         "c3": "C3 mixed: 4096-token prefill + 31 decode tokens, 32 heads, topk 2048",
+         "c4": "C4 fp8 decode: 64 seqs x 1 token, 16 heads, topk 2048, ctx 65536",
+         "c5": f"C5 MTP: 128 seqs x 4 tokens, topk 2048, ctx 32768, {args.kv} KV"}[args.workload]
+    return {"workload": d, "tokens_per_step": w.T, "heads_per_gpu": w.H,
+            "heads_total": heads_total, "topk": w.topk, "kv_rows": int(w.kv.shape[0]),
+            "kv_dtype": "fp8_e4m3" if w.kv.dtype == torch.float8_e4m3fn else "bf16"}
+
+
+# ---------------------------------------------------------------------------
+# measurement helpers
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,"
+              "clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int, enabled: bool = True):
+        self.proc = None
+        self.lines = []
+        self.enabled = enabled
+        self.idx = device_index
+
+    def __enter__(self):
+        if not self.enabled:
+            return self
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.idx), "-lms", "50"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=2)
+
+    def summary(self):
+        rows = []
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 10:
+                continue
+            try:
+                rows.append({"sm": float(parts[1]), "max": float(parts[2]),
+                             "util": float(parts[4]) if parts[4] not in ("[N/A]", "") else 0.0,
+                             "hw": parts[6], "hwt": parts[7], "swt": parts[8], "pcap": parts[9]})
+            except ValueError:
+                continue
+        if not rows:
+            return None
+        busy = [r for r in rows if r["util"] > 0] or rows
+        reasons = []
+        for key, name in (("hw", "hw_slowdown"), ("hwt", "hw_thermal_slowdown"),
+                          ("swt", "sw_thermal_slowdown"), ("pcap", "sw_power_cap")):
+            if any(r[key].lower() == "active" for r in busy):
+                reasons.append(name)
+        return {"sm_mhz": statistics.median(r["sm"] for r in busy),
+                "sm_max_mhz": max(r["max"] for r in rows), "reasons": reasons,
+                "samples": len(rows), "samples_busy": len(busy)}
+
+
+def measured_peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def profiled_traffic(workload: str):
+    """DRAM bytes per launch recorded in the committed ncu summary, if any."""
+    path = os.path.join(REPO, "profiles", f"sparse_mla_fwd_{workload}.md")
+    if not os.path.exists(path):
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9]+)", open(path).read())
+    return int(m.group(1)) if m else None
+
+
+def set_splits(n: int):
+    if n:
+        os.environ["GLM53_SPLITS"] = str(n)
+
+
+# ---------------------------------------------------------------------------
+# arms
+# ---------------------------------------------------------------------------
+def run_ours(args, dist: Dist):
+    torch.cuda.set_device(dist.local)
+    device = torch.device("cuda", dist.local)
+    dist.init("nccl")
+    set_splits(args.splits)
+    import glm53_sparse_mla as G
+    from glm53_sparse_mla import workloads as W
+
+    heads_total = 64 if args.workload in ("c2", "c5") else (32 if args.workload == "c3" else 16)
+    if args.heads:
+        heads_total = args.heads
+    if args.shard == "heads" and dist.world > 1:
+        heads = heads_total // dist.world
+        head_off = heads * dist.rank
+        seed_of = lambda s: 100 + s                       # same batch on every rank
+    else:
+        heads = heads_total
+        head_off = 0
+        seed_of = lambda s: 100 + s + 1000 * dist.rank    # own batch per rank
+    sets = [make_workload(args, W, seed_of(s), device, heads, head_off)
+            for s in range(max(1, args.sets))]
+    w0 = sets[0]
+    outs = [torch.empty_like(w.q) for w in sets]
+    gathered = None
+    if args.allgather and dist.world > 1 and args.shard == "heads":
+        gathered = torch.empty(dist.world, w0.T, heads, 512, dtype=torch.bfloat16, device=device)
+
+    def step(k):
+        w = sets[k % len(sets)]
+        torch.ops.glm53_sparse_mla.sparse_fwd(w.q, w.kv, w.indices, w.sm_scale, w.kv_scale,
+                                              outs[k % len(sets)])
+        if gathered is not None:
+            torch.distributed.all_gather_into_tensor(gathered, outs[k % len(sets)])
+
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        for k in range(max(args.warmup, 3)):
+            step(k)
+    torch.cuda.synchronize()
+
+    # capture the K timed steps in one graph (launch-bound otherwise)
+    graph = torch.cuda.CUDAGraph()
+    use_graph = gathered is None
+    if use_graph:
+        with torch.cuda.graph(graph, stream=stream):
+            for k in range(args.steps):
+                step(k)
+        torch.cuda.synchronize()
+        graph.replay()          # untimed replay: warm the graph launch path
+        torch.cuda.synchronize()
+
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dist.local, enabled=not args.no_clocks) as clk:
+        # soak so the sampler sees the clocks under this load
+        t_end = time.time() + (0.0 if args.no_clocks else 0.5)
+        while time.time() < t_end:
+            (graph.replay() if use_graph else [step(k) for k in range(len(sets))])
+            torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            if use_graph:
+                graph.replay()
+            else:
+                for k in range(args.steps):
+                    step(k)
+            e1.record(stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+    ms_local = e0.elapsed_time(e1)
+    ms = dist.max(ms_local, device)
+    ms_step = ms / args.steps
+    units = w0.T * (dist.world if args.shard == "tokens" else 1)
+    value = units / (ms_step / 1e3)
+
+    # roofline for the attention kernel (per launch on this rank)
+    alg_bytes = w0.algorithmic_bytes()
+    hbm_peak, tf_peak, peak_kind = measured_peaks()
+    achieved = alg_bytes / (ms_local / args.steps / 1e3) / 1e9
+    roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+            "frac": round(achieved / hbm_peak, 4), "peak_source": peak_kind,
+            "traffic": profiled_traffic(args.workload),
+            "algorithmic_bytes_per_launch": alg_bytes,
+            "tensor_tflops": round(w0.flops() / (ms_local / args.steps / 1e3) / 1e12, 1),
+            "tensor_frac": round(w0.flops() / (ms_local / args.steps / 1e3) / 1e12 / tf_peak, 4)}
+    del graph
+    torch.cuda.synchronize()
+
+    # end to end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, G, sets, device, dist)
+
+    cpu = None
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(w0, args.cpu_seconds)
+
+    if dist.rank == 0:
+        cfg = workload_desc(args, w0, heads_total)
+        cfg.update({"parallelism": (f"dp{dist.world}" if args.shard == "tokens"
+                                    else f"tp{dist.world}-heads"),
+                    "l2": f"{len(sets)} rotating input sets, "
+                          f"{sum(w.kv.numel() * w.kv.element_size() for w in sets) / 1e9:.2f} GB "
+                          "of KV pools (>> 126 MB L2); consecutive steps share no memory",
+                    "timing": "K steps in one CUDA graph, CUDA events, max over ranks",
+                    "splits": int(os.environ.get("GLM53_SPLITS", "0")) or "auto",
+                    "allgather": bool(gathered is not None)})
+        line = {"metric": METRIC if args.workload == "c2" else f"sparse-MLA {UNIT} ({args.workload})",
+                "value": round(value, 1), "unit": UNIT, "n_gpus": dist.world, "steps": args.steps,
+                "warmup": max(args.warmup, 3), "ms_per_step": round(ms_step, 5),
+                "higher_is_better": True,
+                "scaling": "weak" if args.shard == "tokens" else "strong",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, random init)",
+                "config": cfg, "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
+                "gpu_launches": args.steps + (args.steps if e2e else 0),
+                "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+    dist.close()
+
+
+def run_e2e(args, G, sets, device, dist: Dist):
+    n = len(sets)
+    q_h = [w.q.cpu().pin_memory() for w in sets]
+    i_h = [w.indices.cpu().pin_memory() for w in sets]
+    o_h = [torch.empty(w.q.shape, dtype=torch.bfloat16).pin_memory() for w in sets]
+    q_d = [torch.empty_like(w.q) for w in sets]
+    i_d = [torch.empty_like(w.indices) for w in sets]
+    o_d = [torch.empty_like(w.q) for w in sets]
+    steps = args.steps
+
+    def step(k):
+        j = k % n
+        w = sets[j]
+        q_d[j].copy_(q_h[j], non_blocking=True)
+        i_d[j].copy_(i_h[j], non_blocking=True)
+        G.sparse_fwd(q_d[j], w.kv, i_d[j], w.sm_scale, w.kv_scale, out=o_d[j])
+        o_h[j].copy_(o_d[j], non_blocking=True)
+
+    for k in range(max(args.warmup, 3)):
+        step(k)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0.record()
+    for k in range(steps):
+        step(k)
+    e1.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    ms = dist.max(e0.elapsed_time(e1), device)
+    w = sets[0]
+    units = w.T * (dist.world if args.shard == "tokens" else 1)
+    return {"value": round(units / (ms / steps / 1e3), 1), "unit": UNIT,
+            "h2d_bytes_per_step": int(w.q.numel() * 2 + w.indices.numel() * 4),
+            "d2h_bytes_per_step": int(w.q.numel() * 2),
+            "ms_per_step": round(ms / steps, 5),
+            "path": "glm53_sparse_mla.sparse_fwd (torch op -> C ABI), pinned host buffers"}
+
+
+def _oracle_inputs(w):
+    from glm53_sparse_mla import workloads as W
+    kv = W.dequantize_fp8(w.kv, w.kv_scale) if w.kv.dtype == torch.float8_e4m3fn else w.kv
+    return (w.q.float().cpu().numpy(), kv.float().cpu().numpy(), w.indices.cpu().numpy())
+
+
+def cpu_baseline(w, seconds: float, heads: int | None = None):
+    """Oracle tokens/s on this host over a bounded sample of the workload."""
+    from oracle import sparse_mla_oracle as O
+    q, kv, idx = _oracle_inputs(w)
+    if heads:
+        q = np.ascontiguousarray(q[:, :heads])
+    try:
+        from threadpoolctl import threadpool_info
+        cores = max((i.get("num_threads", 1) for i in threadpool_info()), default=1)
+    except Exception:  # pragma: no cover
+        cores = os.cpu_count() or 1
+    O.sparse_mla_stats(q[:1], kv, idx[:1], w.sm_scale, chunk=1)    # warm
+    done, t0 = 0, time.perf_counter()
+    while True:
+        j = done % w.T
+        O.sparse_mla_stats(q[j:j + 1], kv, idx[j:j + 1], w.sm_scale, chunk=1)
+        done += 1
+        if time.perf_counter() - t0 >= seconds and done >= 1:
+            break
+    dt = time.perf_counter() - t0
+    frac = (heads or w.H) / w.H
+    return {"value": round(done * frac / dt, 2), "unit": UNIT, "cores": int(cores),
+            "kind": "port",
+            "sample": f"{done} query tokens of the same workload, one at a time"
+                      f"{'' if not heads else f', {heads} of {w.H} heads (scaled)'}"
+                      f", numpy fp32 oracle (restates the reference's tests/reference.py), "
+                      f"{dt:.1f} s"}
+
+
+def run_reference(args, dist: Dist):
+    """Reference arm: the reference's CPU implementation of the path (the
+    oracle port) on the host cores, rank 0 only; other ranks exit at once."""
+    if dist.rank != 0:
+        return
+    from glm53_sparse_mla import workloads as W
+    device = "cuda" if torch.cuda.is_available() else "cpu"
+    w = make_workload(args, W, 100, device, 0)
+    from oracle import sparse_mla_oracle as O
+    q, kv, idx = _oracle_inputs(w)
+    # size each step (one query token; a head slice of it if K is large) so
+    # the whole run stays within about three minutes
+    t0 = time.perf_counter()
+    O.sparse_mla_stats(q[:1], kv, idx[:1], w.sm_scale, chunk=1)
+    t_tok = max(time.perf_counter() - t0, 1e-4)
+    n_total = max(args.steps, 1) + max(args.warmup, 3)
+    heads = w.H
+    while heads > 1 and n_total * t_tok * heads / w.H > 180.0:
+        heads //= 2
+    qs = np.ascontiguousarray(q[:, :heads])
+    for k in range(max(args.warmup, 3)):
+        j = k % w.T
+        O.sparse_mla_stats(qs[j:j + 1], kv, idx[j:j + 1], w.sm_scale, chunk=1)
+    t0 = time.perf_counter()
+    for k in range(args.steps):
+        j = k % w.T
+        O.sparse_mla_stats(qs[j:j + 1], kv, idx[j:j + 1], w.sm_scale, chunk=1)
+    dt = time.perf_counter() - t0
+    value = args.steps * (heads / w.H) / dt
+    try:
+        from threadpoolctl import threadpool_info
+        cores = max((i.get("num_threads", 1) for i in threadpool_info()), default=1)
+    except Exception:  # pragma: no cover
+        cores = os.cpu_count() or 1
+    sample = (f"one query token per step ({heads} of {w.H} heads, scaled), numpy fp32 oracle "
+              "restating the reference's tests/reference.py")
+    line = {"impl": "reference", "metric": METRIC if args.workload == "c2" else
+            f"sparse-MLA {UNIT} ({args.workload})", "value": round(value, 3), "unit": UNIT,
+            "n_gpus": dist.world, "steps": args.steps, "warmup": max(args.warmup, 3),
+            "ms_per_step": round(dt / args.steps * 1e3, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded, random init)",
+            "config": workload_desc(args, w, w.H),
+            "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": int(cores),
+                             "kind": "port", "sample": sample},
+            "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    dist = Dist(args.gpus)
+    if args.impl == "reference":
+        run_reference(args, dist)
+    else:
+        run_ours(args, dist)
+
+
+if __name__ == "__main__":
+    main()

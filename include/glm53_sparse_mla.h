@@ -54,20 +54,23 @@ enum glm53_device_status_bits {
  *   kv       [R, 512]     bf16 or fp8_e4m3 (per-tensor scale kv_scale)
  *   indices  [T, topk]    int32 physical row ids into kv, < 0 = masked
  *   out      [T, H, 512]  bf16, written in place (caller-owned)
- *   lse      [T, H]       fp32 log2-space log-sum-exp, or NULL. A fully masked
- *                         (token, head) gets -inf and an all-zero output row.
+ *   lse      [T, H]       fp32, or NULL: log2(sum_i exp(sm_scale * q . kv_i))
+ *                         over the valid indices. A fully masked (token, head)
+ *                         gets -inf and an all-zero output row.
  *
  * sm_scale is the natural-log softmax scale (the kernel multiplies by log2 e).
  * kv_scale multiplies dequantised fp8 values; it is ignored for bf16.
- * splits: 0 = choose automatically; 1, 2, 4 or 8 = split each token's top-k
- * list across that many CTAs of one thread-block cluster.
+ * splits: 0 = automatic (or the GLM53_SPLITS environment variable, read once);
+ * 1, 2, 4 or 8 = split each token's top-k list across that many CTAs of one
+ * thread-block cluster.
  * H must be 8, 16, 32 or 64; head_dim and the kv width must be 512; topk must
  * be a multiple of 32 and at most 16384. T == 0 is a no-op.
  *
  * Replaces the host launcher `sparse_fwd(q, kv, indices, sm_scale, kv_scale,
  * out)` of the reference (csrc/sparse_mla.cu:455-498) and its launch helper
- * (csrc/sparse_mla.cu:434-453); the lse output has no counterpart there and
- * follows the fp32 oracle's log2 convention (tests/reference.py:71-73).
+ * (csrc/sparse_mla.cu:434-453). The lse output has no counterpart in the
+ * reference op; its fp32 oracle returns a log2 LSE (tests/reference.py:71-73)
+ * whose max term carries sm_scale twice, so the two agree at sm_scale == 1.
  * Launch is asynchronous on `stream`; no host synchronisation, no allocation.
  */
 int glm53_sparse_mla_fwd(const void* q, const void* kv, const int32_t* indices, void* out,

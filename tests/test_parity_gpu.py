@@ -121,12 +121,13 @@ def abi_fwd(lib, w: W.Workload, splits: int, lse: torch.Tensor | None = None):
 
 
 @pytest.mark.parametrize("splits", [1, 2, 4, 8])
-@pytest.mark.parametrize("heads", [64, 8])
+@pytest.mark.parametrize("heads", [64, 32, 16, 8])
 def test_c_abi_explicit_splits(splits, heads):
+    """Every merge path (one CTA per token; 2 or 4 CTAs pushing partials on
+    the bulk-copy engine; 8 CTAs pulling through distributed shared memory)
+    on the whole case matrix, with the LSE output."""
     lib = _abi()
     for w in W.case_matrix(heads=heads, topk=2048, rows=8192, device="cuda"):
-        if w.name not in ("mask_50pct", "row_fully_masked", "tokens_7", "one_tile_masked"):
-            continue
         lse = torch.empty(w.T, w.H, device="cuda")
         out = abi_fwd(lib, w, splits, lse)
         torch.cuda.synchronize()
@@ -135,7 +136,9 @@ def test_c_abi_explicit_splits(splits, heads):
         got = lse.cpu().numpy()
         fin = np.isfinite(ref_lse)
         assert np.array_equal(np.isneginf(got), np.isneginf(ref_lse))
-        assert np.abs(got[fin] - ref_lse[fin]).max() <= LSE_TOL
+        if fin.any():
+            err = np.abs(got[fin] - ref_lse[fin]).max()
+            assert err <= LSE_TOL * max(1.0, np.abs(ref_lse[fin]).max() / 100), (w.name, err)
 
 
 @pytest.mark.parametrize("splits", [1, 2, 4, 8])

@@ -9,10 +9,11 @@
 //   partial results are merged through distributed shared memory at the end,
 //   so no global scratch and no second launch are needed.
 //
-// Per CTA (288 threads, one CTA per SM, ~219 KB shared memory)
+// Per CTA (256 threads, one CTA per SM, ~219 KB shared memory)
 //   warps 0-3  softmax + epilogue  (warp w owns TMEM lanes 32w..32w+31)
-//   warps 4-7  gather              (cp.async 16 B per lane into a 2-stage ring)
-//   warp  8    TMEM allocator + UMMA issuer (one elected lane)
+//   warps 4-6  gather: bf16 KV by 16-byte cp.async, fp8 KV by register loads
+//              + dequantisation, into a 2-stage ring
+//   warp  7    TMEM allocator + UMMA issuer (one lane, event driven)
 //
 // Index handling: the CTA first compacts its chunk of the index list to the
 // valid entries (order preserved), so masked indices cost neither bandwidth
@@ -26,7 +27,10 @@
 //   softmax in the log2 domain on S * (sm_scale * log2 e); P -> smem (bf16).
 //   GEMM2  O^T[d, h] += KV^T[d, i] . P^T[i, h]   M=128 (d, four chunks),
 //          N=NH (heads), K=64; A=KV read MN-major from the same smem tile,
-//          B=P K-major; O^T accumulates in TMEM across all tiles.
+//          B=P K-major; O^T accumulates in TMEM across all tiles. The four
+//          d-chunks are issued interleaved so consecutive UMMAs are independent.
+// The UMMA issuer runs GEMM2(t) as soon as P(t) is ready (it frees a stage)
+// and GEMM1(t+1) as soon as its rows have landed.
 // The running max only moves when a head's tile max exceeds it by more than
 // 2^8; then the O^T columns of the moved heads are rescaled in TMEM.
 //
@@ -34,6 +38,9 @@
 // stored as 64-element (128 B) column blocks; inside a block, row r sits at
 // r * 128 and its 16-byte chunk c at ((c ^ (r % 8)) * 16). The KV tile serves
 // GEMM1 as a K-major operand and GEMM2 as an MN-major one without re-layout.
+// (A TMA tile::gather4 of the same layout was measured at ~90 cycles per
+// 512-byte instruction issue on this part, well below the gather rate needed,
+// so the gather uses cp.async.)
 //
 // Every pipeline wait is bounded in wall time; on expiry the CTA raises a
 // device status bit, finishes without further waiting and releases its TMEM.
@@ -56,9 +63,11 @@ namespace glm53 {
 constexpr int kDim = 512;           // latent width = head size
 constexpr int kRows = 64;           // KV rows per pipeline tile
 constexpr int kMaxChunk = 2048;     // indices one CTA can hold after compaction
-constexpr int kThreads = 288;       // 9 warps
-constexpr int kProducerWarp0 = 4;   // warps 4-7 gather
-constexpr int kMmaWarp = 8;
+constexpr int kThreads = 256;       // 8 warps (a 288-thread CTA caps registers at 168)
+constexpr int kProducerWarp0 = 4;   // warps 4-6 gather
+constexpr int kProducerWarps = 3;
+constexpr int kProducerThreads = 32 * kProducerWarps;
+constexpr int kMmaWarp = 7;
 constexpr int kTmemCols = 512;
 constexpr uint32_t kTmemS = 256;    // S double buffer at columns 256 and 320
 constexpr float kRescaleThreshold = 8.0f;   // log2 units: rescale when max grows > 256x
@@ -85,7 +94,8 @@ enum : int {
   kBarPFull = 8,     // [2] softmax -> MMA: P written (and O rescaled)
   kBarODone = 10,    // MMA (commit) -> softmax: a GEMM2 finished
   kBarDrain = 11,    // MMA (commit) -> MMA: every UMMA finished
-  kNumBars = 12
+  kBarQFull = 12,    // all threads (cp.async) -> MMA: Q landed
+  kNumBars = 13
 };
 
 // misc words
@@ -151,6 +161,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
   const int lane = tid & 31;
   const int split = static_cast<int>(blockIdx.x) % p.splits;
   const int token = static_cast<int>(blockIdx.x) / p.splits;
+  const int nranks = p.splits;
 
   float* const m_sm = reinterpret_cast<float*>(gb + kSmHead);
   float* const l_sm = m_sm + 64;
@@ -163,18 +174,16 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
 
   // ------------------------------------------------------------------ setup
   if (tid == 0) {
-    mbar_init(bar(kBarKvFull + 0), 128);
-    mbar_init(bar(kBarKvFull + 1), 128);
-    mbar_init(bar(kBarKvEmpty + 0), 1);
-    mbar_init(bar(kBarKvEmpty + 1), 1);
-    mbar_init(bar(kBarSFull + 0), 1);
-    mbar_init(bar(kBarSFull + 1), 1);
-    mbar_init(bar(kBarSEmpty + 0), 128);
-    mbar_init(bar(kBarSEmpty + 1), 128);
-    mbar_init(bar(kBarPFull + 0), 128);
-    mbar_init(bar(kBarPFull + 1), 128);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar(kBarKvFull + s), kProducerThreads);
+      mbar_init(bar(kBarKvEmpty + s), 1);
+      mbar_init(bar(kBarSFull + s), 1);
+      mbar_init(bar(kBarSEmpty + s), 128);
+      mbar_init(bar(kBarPFull + s), 128);
+    }
     mbar_init(bar(kBarODone), 1);
     mbar_init(bar(kBarDrain), 1);
+    mbar_init(bar(kBarQFull), kThreads);
     misc[kMiscAbort] = 0;
     fence_mbarrier_init();
   }
@@ -182,16 +191,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
     tmem_alloc(sb + kSmMisc + 4 * kMiscTmem, kTmemCols);
     tmem_relinquish();
   }
-
-  // Q (all 64 rows of the M=64 operand; rows >= H are zero) via cp.async.
-  {
-    const __nv_bfloat16* qtok = p.q + static_cast<size_t>(token) * p.H * kDim;
-    for (int u = tid; u < 64 * 64; u += kThreads) {
-      const int h = u >> 6, c = u & 63;
-      const bool ok = h < p.H;
-      cp_async_16(sb + kSmQ + swz(h, c), qtok + (ok ? h : 0) * kDim + c * 8, ok ? 16u : 0u);
-    }
-  }
+  __syncthreads();   // barriers initialised before anyone arrives on them
 
   // Index compaction, pass 1: warps 0-7 each take a contiguous sub-range of
   // this CTA's chunk, keep it in registers and count the valid entries.
@@ -218,8 +218,18 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
     if (lane == 0) misc[kMiscWarpCount + warp] = static_cast<uint32_t>(cnt);
     if (bad) atomicOr(&g_device_status, static_cast<unsigned>(GLM53_DEV_BAD_INDEX));
   }
-  cp_async_wait_all();
-  fence_proxy_async_smem();   // Q bytes written by cp.async -> tensor-core reads
+  // Q (all 64 rows of the M=64 operand; rows >= H are zero) via cp.async,
+  // issued after the index loads so those are not queued behind it; its
+  // arrival is tracked by its own barrier so the KV gather never waits on it.
+  {
+    const __nv_bfloat16* qtok = p.q + static_cast<size_t>(token) * p.H * kDim;
+    for (int u = tid; u < 64 * 64; u += kThreads) {
+      const int h = u >> 6, c = u & 63;
+      const bool ok = h < p.H;
+      cp_async_16(sb + kSmQ + swz(h, c), qtok + (ok ? h : 0) * kDim + c * 8, ok ? 16u : 0u);
+    }
+    cp_async_mbar_arrive_noinc(bar(kBarQFull));
+  }
   __syncthreads();
 
   // pass 2: scatter the valid entries to their compacted positions
@@ -248,17 +258,20 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
   if (warp >= kProducerWarp0 && warp < kMmaWarp) {
     // ================= gather =================
     const int pw = warp - kProducerWarp0;
-    for (int t = 0; t < n_tiles; ++t) {
-      const int s = t & 1;
-      if (t >= 2 &&
-          !mbar_wait_bounded(bar(kBarKvEmpty + s), ((t >> 1) - 1) & 1, abort_flag, p.timeout_ns))
-        break;
-      const uint32_t stage = sb + kSmKV + s * kStageBytes;
-      const int rows = min(kRows, n_valid - kRows * t);
-      if constexpr (!kFp8) {
-        const uint8_t* kvb = static_cast<const uint8_t*>(p.kv);
+    if constexpr (!kFp8) {
+      // 16-byte cp.async per lane, half a row per warp instruction; the
+      // deferred arrive (.noinc) completes the stage once this thread's copies
+      // land. The last tile's missing rows are zero-filled (src-size 0).
+      const uint8_t* kvb = static_cast<const uint8_t*>(p.kv);
+      for (int t = 0; t < n_tiles; ++t) {
+        const int s = t & 1;
+        if (t >= 2 &&
+            !mbar_wait_bounded(bar(kBarKvEmpty + s), ((t >> 1) - 1) & 1, abort_flag, p.timeout_ns))
+          break;
+        const uint32_t stage = sb + kSmKV + s * kStageBytes;
+        const int rows = min(kRows, n_valid - kRows * t);
 #pragma unroll 4
-        for (int r = pw; r < kRows; r += 4) {
+        for (int r = pw; r < kRows; r += kProducerWarps) {
           const bool valid = r < rows;
           const long long row = valid ? idx_sm[kRows * t + r] : 0;
           const uint8_t* src = kvb + row * (kDim * 2);
@@ -269,12 +282,21 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
           }
         }
         cp_async_mbar_arrive_noinc(bar(kBarKvFull + s));
-      } else {
-        const uint8_t* kv8 = static_cast<const uint8_t*>(p.kv);
-        uint4 buf[16];
+      }
+    } else {
+      const uint8_t* kv8 = static_cast<const uint8_t*>(p.kv);
+      for (int t = 0; t < n_tiles; ++t) {
+        const int s = t & 1;
+        if (t >= 2 &&
+            !mbar_wait_bounded(bar(kBarKvEmpty + s), ((t >> 1) - 1) & 1, abort_flag, p.timeout_ns))
+          break;
+        const uint32_t stage = sb + kSmKV + s * kStageBytes;
+        const int rows = min(kRows, n_valid - kRows * t);
+        constexpr int kPer = (kRows + kProducerWarps - 1) / kProducerWarps;
+        uint4 buf[kPer];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int r = pw + 4 * j;
+        for (int j = 0; j < kPer; ++j) {
+          const int r = pw + kProducerWarps * j;
           if (r < rows) {
             const long long row = idx_sm[kRows * t + r];
             buf[j] = ldg_nc_v4(kv8 + row * kDim + lane * 16);
@@ -283,8 +305,9 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
           }
         }
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int r = pw + 4 * j;
+        for (int j = 0; j < kPer; ++j) {
+          const int r = pw + kProducerWarps * j;
+          if (r >= kRows) break;
           uint4 lo, hi;
           dequant16(buf[j], p.kv_scale, lo, hi);
           sts_v4(stage + swz(r, 2 * lane), lo);
@@ -294,68 +317,80 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
         mbar_arrive(bar(kBarKvFull + s));
       }
     }
-    cp_async_wait_all();
     __syncwarp();
   } else if (warp == kMmaWarp) {
     // ================= UMMA issue =================
     if (lane == 0) {
       constexpr uint32_t kIdesc1 = idesc_bf16_f32(64, 64, false, false);
       constexpr uint32_t kIdesc2 = idesc_bf16_f32(128, NH, true, false);
-      auto gemm1 = [&](int t) {
+      // GEMM1 of tile g1 is 32 K-steps into S; GEMM2 of tile g2 is 4 K-steps
+      // x 4 d-chunks into O^T, chunks innermost so consecutive UMMAs are
+      // independent. Readiness is probed only between issue sequences: a
+      // barrier probe between UMMAs stalls the issuing thread. When both are
+      // ready, the GEMM2 steps are paired with the first 16 GEMM1 steps and
+      // committed at once (freeing the stage early), then GEMM1 finishes.
+      auto gemm1_step = [=](int t, int kk) {
         const uint32_t stage = sb + kSmKV + (t & 1) * kStageBytes;
-        const uint32_t d_tmem = tmem + kTmemS + 64u * (t & 1);
-#pragma unroll
-        for (int kk = 0; kk < kDim / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * 8192u + (kk & 3) * 32u;
-          umma_bf16(d_tmem, sdesc_sw128(sb + kSmQ + off, 16, 1024),
-                    sdesc_sw128(stage + off, 16, 1024), kIdesc1, kk > 0 ? 1u : 0u);
-        }
+        const uint32_t off = (kk >> 2) * 8192u + (kk & 3) * 32u;
+        umma_bf16(tmem + kTmemS + 64u * (t & 1), sdesc_sw128(sb + kSmQ + off, 16, 1024),
+                  sdesc_sw128(stage + off, 16, 1024), kIdesc1, kk > 0 ? 1u : 0u);
       };
-      auto gemm2 = [&](int t) {
+      auto gemm2_step = [=](int t, int i) {
+        const int kk = i >> 2, m = i & 3;
         const uint32_t stage = sb + kSmKV + (t & 1) * kStageBytes;
         const uint32_t pbuf = sb + kSmP + (t & 1) * kPBytes;
-#pragma unroll
-        for (int m = 0; m < 4; ++m) {
-#pragma unroll
-          for (int kk = 0; kk < kRows / 16; ++kk) {
-            umma_bf16(tmem + static_cast<uint32_t>(m * NH),
-                      sdesc_sw128(stage + m * 16384u + kk * 2048u, 8192, 1024),
-                      sdesc_sw128(pbuf + kk * 32u, 16, 1024), kIdesc2,
-                      (t > 0 || kk > 0) ? 1u : 0u);
-          }
-        }
+        umma_bf16(tmem + static_cast<uint32_t>(m * NH),
+                  sdesc_sw128(stage + m * 16384u + kk * 2048u, 8192, 1024),
+                  sdesc_sw128(pbuf + kk * 32u, 16, 1024), kIdesc2, (t > 0 || kk > 0) ? 1u : 0u);
       };
-      bool ok = true;
-      for (int t = 0; t < n_tiles && ok; ++t) {
-        const int s = t & 1;
-        ok = mbar_wait_bounded(bar(kBarKvFull + s), (t >> 1) & 1, abort_flag, p.timeout_ns);
-        if (!ok) break;
-        fence_proxy_async_smem();
-        if (t >= 2) {
-          ok = mbar_wait_bounded(bar(kBarSEmpty + s), ((t >> 1) - 1) & 1, abort_flag,
-                                 p.timeout_ns);
-          if (!ok) break;
+      constexpr int kSteps1 = kDim / 16;          // 32
+      constexpr int kSteps2 = (kRows / 16) * 4;   // 16
+      bool ok = n_tiles == 0 || mbar_wait_bounded(bar(kBarQFull), 0, abort_flag, p.timeout_ns);
+      fence_proxy_async_smem();   // Q written by cp.async -> tensor-core reads
+      int g1 = 0, g2 = 0;         // next tile for GEMM1 / GEMM2
+      uint64_t t_idle = 0;
+      while (ok && g2 < n_tiles) {
+        const bool ready2 = g2 < g1 && mbar_test_wait(bar(kBarPFull + (g2 & 1)), (g2 >> 1) & 1);
+        const bool ready1 = g1 < n_tiles && g1 < g2 + 2 &&
+                            mbar_test_wait(bar(kBarKvFull + (g1 & 1)), (g1 >> 1) & 1) &&
+                            (g1 < 2 || mbar_test_wait(bar(kBarSEmpty + (g1 & 1)), ((g1 >> 1) - 1) & 1));
+        if (!ready1 && !ready2) {
+          if (*abort_flag) {
+            ok = false;
+          } else {
+            const uint64_t now = global_timer_ns();
+            if (t_idle == 0) {
+              t_idle = now;
+            } else if (now - t_idle > p.timeout_ns) {
+              *abort_flag = 1;
+              ok = false;
+            }
+          }
+          continue;
         }
+        t_idle = 0;
+        if (ready1) fence_proxy_async_smem();   // generic-proxy smem writes -> tensor-core reads
         tc_fence_after();
-        gemm1(t);
-        umma_commit(bar(kBarSFull + s));
-        if (t >= 1) {
-          const int u = t - 1;
-          ok = mbar_wait_bounded(bar(kBarPFull + (u & 1)), (u >> 1) & 1, abort_flag, p.timeout_ns);
-          if (!ok) break;
-          tc_fence_after();
-          gemm2(u);
-          umma_commit(bar(kBarKvEmpty + (u & 1)));
+        if (ready2) {
+#pragma unroll
+          for (int i = 0; i < kSteps2; ++i) {
+            gemm2_step(g2, i);
+            if (ready1) gemm1_step(g1, i);
+          }
+          umma_commit(bar(kBarKvEmpty + (g2 & 1)));
           umma_commit(bar(kBarODone));
-        }
-      }
-      if (ok && n_tiles > 0) {
-        const int u = n_tiles - 1;
-        if (mbar_wait_bounded(bar(kBarPFull + (u & 1)), (u >> 1) & 1, abort_flag, p.timeout_ns)) {
-          tc_fence_after();
-          gemm2(u);
-          umma_commit(bar(kBarKvEmpty + (u & 1)));
-          umma_commit(bar(kBarODone));
+          ++g2;
+          if (ready1) {
+#pragma unroll
+            for (int i = kSteps2; i < kSteps1; ++i) gemm1_step(g1, i);
+            umma_commit(bar(kBarSFull + (g1 & 1)));
+            ++g1;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < kSteps1; ++i) gemm1_step(g1, i);
+          umma_commit(bar(kBarSFull + (g1 & 1)));
+          ++g1;
         }
       }
       // Drain: never release TMEM while a UMMA may still write it.
@@ -364,7 +399,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
       mbar_wait_bounded(bar(kBarDrain), 0, &no_abort, p.timeout_ns);
     }
     __syncwarp();
-  } else {
+  } else if (warp < 4) {
     // ================= softmax (warps 0-3) =================
     const int q4 = warp;                       // TMEM lane quadrant
     const int h = 16 * q4 + (lane & 15);       // head owned (M=64 layout)
@@ -434,8 +469,6 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
           }
         }
         tmem_wait_st();
-        // alpha_sm is rewritten only after the next p_full wait of the MMA
-        // warp, which this group's arrive below gates; nothing else to order.
       }
       l_part *= alpha;
       m_used = new_m;
@@ -464,7 +497,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
       mbar_arrive(bar(kBarPFull + b));
     }
 
-    // publish this CTA's per-head max and sum for the cluster merge
+    // publish this CTA's per-head max and sum for the merge
     __syncwarp();
     const float l_tot = l_part + __shfl_xor_sync(0xFFFFFFFFu, l_part, 16);
     if (has_head && half == 0) {
@@ -474,64 +507,225 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
   }
 
   // ------------------------------------------------------------------ merge
-  const int nranks = p.splits;
-  cluster_sync_all();   // (A) every CTA's m/l visible cluster-wide
+  const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
+  __nv_bfloat16* const o_tok = p.out + static_cast<size_t>(token) * p.H * kDim;
+  const bool odd = lane & 1;
 
-  if (warp < 4) {
-    if (tid < NH) {
-      const int hh = tid;
-      const uint32_t m_addr = sb + kSmHead + 4u * hh;
-      const uint32_t l_addr = m_addr + 256u;
-      float M = -INFINITY;
-      for (int r = 0; r < nranks; ++r) {
-        const float lr = ld_dsmem_f32(mapa_shared(l_addr, r));
-        if (lr > 0.f) M = fmaxf(M, ld_dsmem_f32(mapa_shared(m_addr, r)));
+  // O^T[d][0..NH) of TMEM lane d of chunk m (all loads issued, one wait)
+  auto load_o = [=](int m, float (&o)[NH]) {
+    if constexpr (NH == 16) {
+      tmem_ld_32x32b_x16(tmem + lane_base + static_cast<uint32_t>(m * NH), o);
+      tmem_wait_ld();
+    } else {
+#pragma unroll
+      for (int cc = 0; cc < NH / 32; ++cc) {
+        float o32[32];
+        tmem_ld_32x32b_x32(tmem + lane_base + static_cast<uint32_t>(m * NH + 32 * cc), o32);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) o[32 * cc + j] = o32[j];
       }
-      float L = 0.f;
-      for (int r = 0; r < nranks; ++r) {
-        const float lr = ld_dsmem_f32(mapa_shared(l_addr, r));
-        if (lr > 0.f) L += lr * exp2f(ld_dsmem_f32(mapa_shared(m_addr, r)) - M);
-      }
-      const float l_own = l_sm[hh];
-      f_sm[hh] = (L > 0.f && l_own > 0.f) ? exp2f(m_sm[hh] - M) / L : 0.f;
-      if (split == 0 && p.lse != nullptr && hh < p.H)
-        p.lse[static_cast<size_t>(token) * p.H + hh] = L > 0.f ? log2f(L) + M : -INFINITY;
+      tmem_wait_ld();
     }
-    named_bar_sync(1, 128);
+  };
+  // bf16 store of out[h][d] for all heads of this lane's d: neighbouring lanes
+  // swap one value per head pair so each lane writes a bf16x2 of two d
+  auto store_pairs = [=](int d, const float (&o)[NH]) {
+    const int d_even = d & ~1;
+#pragma unroll
+    for (int j = 0; j < NH; j += 2) {
+      const float recv = __shfl_xor_sync(0xFFFFFFFFu, odd ? o[j] : o[j + 1], 1);
+      const int hw = odd ? j + 1 : j;
+      const uint32_t pair = odd ? pack_bf16x2(recv, o[j + 1]) : pack_bf16x2(o[j], recv);
+      if (hw < p.H)
+        *reinterpret_cast<uint32_t*>(o_tok + static_cast<size_t>(hw) * kDim + d_even) = pair;
+    }
+  };
 
-    // scaled partial O^T -> fp32 [NH][512] in the (now idle) KV stage region
-    if (n_tiles > 0)
-      mbar_wait_bounded(bar(kBarODone), (n_tiles - 1) & 1, abort_flag, p.timeout_ns);
-    tc_fence_after();
-    float* const part = reinterpret_cast<float*>(gb + kSmKV);
-    const uint32_t lane_base = static_cast<uint32_t>(32 * warp) << 16;
+  if (nranks == 1) {
+    // ---- single CTA per token: normalise and store straight from TMEM
+    __syncthreads();
+    if (warp < 4) {
+      if (tid < NH) {
+        const float L = l_sm[tid];
+        f_sm[tid] = L > 0.f ? 1.f / L : 0.f;
+        if (p.lse != nullptr && tid < p.H)
+          p.lse[static_cast<size_t>(token) * p.H + tid] = L > 0.f ? log2f(L) + m_sm[tid] : -INFINITY;
+      }
+      named_bar_sync(1, 128);
+      if (n_tiles > 0)
+        mbar_wait_bounded(bar(kBarODone), (n_tiles - 1) & 1, abort_flag, p.timeout_ns);
+      tc_fence_after();
+#pragma unroll 1
+      for (int m = 0; m < 4; ++m) {
+        float o[NH];
+        load_o(m, o);
 #pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      const int d = 128 * m + 32 * warp + lane;
-      if constexpr (NH == 16) {
-        float o[16];
-        tmem_ld_32x32b_x16(tmem + lane_base + static_cast<uint32_t>(m * NH), o);
-        tmem_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 16; ++j) part[j * kDim + d] = n_tiles > 0 ? o[j] * f_sm[j] : 0.f;
-      } else {
-#pragma unroll
-        for (int cc = 0; cc < NH / 32; ++cc) {
-          float o[32];
-          tmem_ld_32x32b_x32(tmem + lane_base + static_cast<uint32_t>(m * NH + 32 * cc), o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            part[(32 * cc + j) * kDim + d] = n_tiles > 0 ? o[j] * f_sm[32 * cc + j] : 0.f;
+        for (int j = 0; j < NH; ++j) o[j] = n_tiles > 0 ? o[j] * f_sm[j] : 0.f;
+        store_pairs(128 * m + 32 * warp + lane, o);
+      }
+      tc_fence_before();
+    }
+    __syncthreads();
+  } else if (nranks <= 4) {
+    // ---- split across 2 or 4 CTAs: each CTA owns a d-slice of the output.
+    // After a cluster barrier (every CTA past its main loop, so receive
+    // buffers are free), each CTA stores, into every peer's receive slot, its
+    // per-head (max, sum) and its unscaled partial for that peer's slice; a
+    // second barrier publishes the stores and each owner combines them with
+    // its own partial, read straight from TMEM. Slot layout: m[NH], l[NH],
+    // then one row of NH floats per d of the slice, its 16-byte chunks XOR-
+    // swizzled by the row index (within groups of up to 8 chunks) so a warp
+    // reading 32 consecutive rows spreads over all banks.
+    const int dspan = kDim / nranks;                                 // 256 or 128
+    const uint32_t slot_bytes = 4u * (2u * NH + static_cast<uint32_t>(NH * dspan));
+    const uint32_t recv_base = sb;                                   // (nranks-1) slots
+    float* const scal = reinterpret_cast<float*>(gb + kSmIdx);       // e[4][NH], 1/L[NH]
+    constexpr int kSw = NH / 4 < 8 ? NH / 4 : 8;   // chunks per swizzle group (row = NH/4 chunks)
+    auto row_chunk = [](int row, int c) { return (c & ~(kSw - 1)) | ((c ^ row) & (kSw - 1)); };
+    cluster_sync_all();   // every CTA is past its main loop
+    if (warp < 4) {
+      if (n_tiles > 0)
+        mbar_wait_bounded(bar(kBarODone), (n_tiles - 1) & 1, abort_flag, p.timeout_ns);
+      tc_fence_after();
+      if (tid < NH) {
+        for (int q = 0; q < nranks; ++q) {
+          if (q == split) continue;
+          const uint32_t rslot = recv_base + (split < q ? split : split - 1) * slot_bytes;
+          st_dsmem_f32(mapa_shared(rslot + 4u * tid, q), m_sm[tid]);
+          st_dsmem_f32(mapa_shared(rslot + 4u * (NH + tid), q), l_sm[tid]);
         }
       }
+#pragma unroll 1
+      for (int m = 0; m < 4; ++m) {
+        const int d = 128 * m + 32 * warp + lane;
+        const int owner = d / dspan;
+        if (owner == split) continue;            // own slice stays in TMEM
+        float o[NH];
+        if (n_tiles > 0) {
+          load_o(m, o);
+        } else {
+#pragma unroll
+          for (int j = 0; j < NH; ++j) o[j] = 0.f;
+        }
+        const int dl = d - owner * dspan;
+        const uint32_t row = mapa_shared(recv_base + (split < owner ? split : split - 1) * slot_bytes +
+                                             4u * (2 * NH + dl * NH), owner);
+#pragma unroll
+        for (int c = 0; c < NH / 4; ++c)
+          st_dsmem_v4(row + 16u * row_chunk(dl, c),
+                      make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]));
+      }
+      tc_fence_before();
     }
-    tc_fence_before();
-  }
-  cluster_sync_all();   // (B) every CTA's scaled partial visible cluster-wide
-
-  // Each CTA of the cluster sums one d-slice over all ranks and writes bf16.
-  {
+    cluster_sync_all();   // every peer's stores into this CTA are visible
+    if (warp < 4) {
+      if (tid < NH) {
+        // ranks in order; own (max, sum) from local smem, others from slots
+        float mr[4], lr[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          if (r < nranks) {
+            if (r == split) {
+              mr[r] = m_sm[tid];
+              lr[r] = l_sm[tid];
+            } else {
+              const float* slot = reinterpret_cast<const float*>(gb + (r < split ? r : r - 1) * slot_bytes);
+              mr[r] = slot[tid];
+              lr[r] = slot[NH + tid];
+            }
+          }
+        }
+        float M = -INFINITY;
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+          if (r < nranks && lr[r] > 0.f) M = fmaxf(M, mr[r]);
+        float L = 0.f, e[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          e[r] = (r < nranks && lr[r] > 0.f) ? exp2f(mr[r] - M) : 0.f;
+          if (r < nranks) L += lr[r] * e[r];
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r) scal[r * NH + tid] = e[r];
+        scal[4 * NH + tid] = L > 0.f ? 1.f / L : 0.f;
+        if (split == 0 && p.lse != nullptr && tid < p.H)
+          p.lse[static_cast<size_t>(token) * p.H + tid] = L > 0.f ? log2f(L) + M : -INFINITY;
+      }
+      named_bar_sync(1, 128);
+#pragma unroll 1
+      for (int mm = 0; mm < 4 / nranks; ++mm) {
+        const int m = split * (4 / nranks) + mm;
+        const int d = 128 * m + 32 * warp + lane;
+        const int dl = d - split * dspan;
+        float o[NH];
+        if (n_tiles > 0) {
+          load_o(m, o);
+        } else {
+#pragma unroll
+          for (int j = 0; j < NH; ++j) o[j] = 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < NH; ++j) o[j] *= scal[split * NH + j];
+        for (int r = 0; r < nranks; ++r) {
+          if (r == split) continue;
+          const float4* row = reinterpret_cast<const float4*>(
+              gb + (r < split ? r : r - 1) * slot_bytes + 4u * (2 * NH + dl * NH));
+#pragma unroll
+          for (int c = 0; c < NH / 4; ++c) {
+            const float4 v = row[row_chunk(dl, c)];
+            o[4 * c] += v.x * scal[r * NH + 4 * c];
+            o[4 * c + 1] += v.y * scal[r * NH + 4 * c + 1];
+            o[4 * c + 2] += v.z * scal[r * NH + 4 * c + 2];
+            o[4 * c + 3] += v.w * scal[r * NH + 4 * c + 3];
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < NH; ++j) o[j] *= scal[4 * NH + j];
+        store_pairs(d, o);
+      }
+      tc_fence_before();
+    }
+    __syncthreads();
+  } else {
+    // ---- split across 8 CTAs (tiny batches): merge through distributed
+    // shared memory reads
+    cluster_sync_all();   // (A) every CTA's m / l visible cluster-wide
+    if (warp < 4) {
+      if (tid < NH) {
+        const int hh = tid;
+        const uint32_t m_addr = sb + kSmHead + 4u * hh;
+        const uint32_t l_addr = m_addr + 256u;
+        float M = -INFINITY, L = 0.f;
+        for (int r = 0; r < nranks; ++r) {
+          const float lr = ld_dsmem_f32(mapa_shared(l_addr, r));
+          if (lr > 0.f) M = fmaxf(M, ld_dsmem_f32(mapa_shared(m_addr, r)));
+        }
+        for (int r = 0; r < nranks; ++r) {
+          const float lr = ld_dsmem_f32(mapa_shared(l_addr, r));
+          if (lr > 0.f) L += lr * exp2f(ld_dsmem_f32(mapa_shared(m_addr, r)) - M);
+        }
+        const float l_own = l_sm[hh];
+        f_sm[hh] = (L > 0.f && l_own > 0.f) ? exp2f(m_sm[hh] - M) / L : 0.f;
+        if (split == 0 && p.lse != nullptr && hh < p.H)
+          p.lse[static_cast<size_t>(token) * p.H + hh] = L > 0.f ? log2f(L) + M : -INFINITY;
+      }
+      named_bar_sync(1, 128);
+      if (n_tiles > 0)
+        mbar_wait_bounded(bar(kBarODone), (n_tiles - 1) & 1, abort_flag, p.timeout_ns);
+      tc_fence_after();
+      // scaled partial -> fp32 [h][512] in the (now idle) KV stage region
+      float* const part = reinterpret_cast<float*>(gb + kSmKV);
+#pragma unroll 1
+      for (int m = 0; m < 4; ++m) {
+        const int d = 128 * m + 32 * warp + lane;
+        float o[NH];
+        load_o(m, o);
+#pragma unroll
+        for (int j = 0; j < NH; ++j) part[j * kDim + d] = n_tiles > 0 ? o[j] * f_sm[j] : 0.f;
+      }
+      tc_fence_before();
+    }
+    cluster_sync_all();   // (B) every CTA's scaled partial visible cluster-wide
     const int dspan = kDim / nranks;
     const int units_per_head = dspan / 8;
     const int units = p.H * units_per_head;
@@ -539,21 +733,27 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
       const int hh = u / units_per_head;
       const int d = split * dspan + (u % units_per_head) * 8;
       const uint32_t off = sb + kSmKV + static_cast<uint32_t>(hh * kDim + d) * 4u;
-      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (int r = 0; r < nranks; ++r) {
+      float4 x[8], y[8];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
         const uint32_t a = mapa_shared(off, r);
-        const float4 x = ld_dsmem_v4(a);
-        const float4 y = ld_dsmem_v4(a + 16);
-        acc[0] += x.x; acc[1] += x.y; acc[2] += x.z; acc[3] += x.w;
-        acc[4] += y.x; acc[5] += y.y; acc[6] += y.z; acc[7] += y.w;
+        x[r] = ld_dsmem_v4(a);
+        y[r] = ld_dsmem_v4(a + 16);
       }
-      stg_v4(p.out + (static_cast<size_t>(token) * p.H + hh) * kDim + d,
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        acc[0] += x[r].x; acc[1] += x[r].y; acc[2] += x[r].z; acc[3] += x[r].w;
+        acc[4] += y[r].x; acc[5] += y[r].y; acc[6] += y[r].z; acc[7] += y[r].w;
+      }
+      stg_v4(o_tok + static_cast<size_t>(hh) * kDim + d,
              make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
                         pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7])));
     }
+    cluster_sync_all();   // (C) no CTA leaves while a peer still reads its smem
   }
-  cluster_sync_all();   // (C) no CTA leaves while a peer still reads its smem
 
+  cp_async_wait_all();
   if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
@@ -608,6 +808,7 @@ bool g_prepared[kMaxDevices] = {};
 int g_sm_count[kMaxDevices] = {};
 int g_cc_major[kMaxDevices] = {};
 unsigned long long g_timeout_ns = 0;
+int g_env_splits = -1;   // GLM53_SPLITS: forced split count for splits == 0 (-1: unread)
 
 template <int NH, bool FP8>
 cudaError_t launch_fwd(const Params& p, int splits, cudaStream_t stream) {
@@ -640,6 +841,11 @@ int prepare_current_device(int* dev_out) {
   if (dev_out) *dev_out = dev;
   std::lock_guard<std::mutex> lock(g_mutex);
   if (g_prepared[dev]) return GLM53_OK;
+  if (g_env_splits < 0) {
+    const char* env = std::getenv("GLM53_SPLITS");
+    const int v = env ? std::atoi(env) : 0;
+    g_env_splits = (v == 1 || v == 2 || v == 4 || v == 8) ? v : 0;
+  }
   if (g_timeout_ns == 0) {
     const char* env = std::getenv("GLM53_WAIT_TIMEOUT_MS");
     const long long ms = env ? std::atoll(env) : 0;
@@ -712,7 +918,8 @@ extern "C" int glm53_sparse_mla_fwd(const void* q, const void* kv, const int32_t
   int dev = 0;
   rc = prepare_current_device(&dev);
   if (rc != GLM53_OK) return rc;
-  const int s = splits != 0 ? splits : glm53_sparse_mla_auto_splits(T, topk, g_sm_count[dev]);
+  int s = splits;
+  if (s == 0) s = g_env_splits > 0 ? g_env_splits : glm53_sparse_mla_auto_splits(T, topk, g_sm_count[dev]);
   if ((topk + s - 1) / s > kMaxChunk) return GLM53_ERR_TOPK;
 
   Params p;

@@ -303,6 +303,13 @@ class Glm53SparseMLAImpl(MLAAttentionImpl[Glm53SparseMLAMetadata]):
             return 1.0
         return float(s.item()) if torch.is_tensor(s) else float(s)
 
+    def forward_mha(self, q, kv_c_normed, k_pe, kv_c_and_k_pe_cache, attn_metadata, k_scale,
+                    output) -> None:
+        # The builder reports every token as a decode token, so the shared MLA
+        # layer never takes its dense-MHA branch; vLLM versions that declare
+        # this method abstract still need it defined.
+        raise NotImplementedError("glm53 sparse MLA runs every token through forward_mqa")
+
     def forward_mqa(
         self,
         q: torch.Tensor | tuple[torch.Tensor, torch.Tensor],
