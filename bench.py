@@ -245,14 +245,14 @@ def run_ours(args, dist: Dist):
     dist.init("nccl")
     set_splits(args.splits)
     import glm53_sparse_mla as G
+    from glm53_sparse_mla import sharding as S
     from glm53_sparse_mla import workloads as W
 
     heads_total = 64 if args.workload in ("c2", "c5") else (32 if args.workload == "c3" else 16)
     if args.heads:
         heads_total = args.heads
     if args.shard == "heads" and dist.world > 1:
-        heads = heads_total // dist.world
-        head_off = heads * dist.rank
+        head_off, heads = S.head_range(dist.rank, dist.world, heads_total)
         seed_of = lambda s: 100 + s                       # same batch on every rank
     else:
         heads = heads_total
@@ -271,7 +271,7 @@ def run_ours(args, dist: Dist):
         torch.ops.glm53_sparse_mla.sparse_fwd(w.q, w.kv, w.indices, w.sm_scale, w.kv_scale,
                                               outs[k % len(sets)])
         if gathered is not None:
-            torch.distributed.all_gather_into_tensor(gathered, outs[k % len(sets)])
+            S.gather_heads(outs[k % len(sets)], dist.world, staging=gathered)
 
     stream = torch.cuda.Stream(device)
     with torch.cuda.stream(stream):

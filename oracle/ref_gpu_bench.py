@@ -45,6 +45,7 @@ def main():
     spec = importlib.util.spec_from_file_location(
         "wl", os.path.join(REPO, "vllm-sparse-mla-blackwell_b200", "glm53_sparse_mla", "workloads.py"))
     W = importlib.util.module_from_spec(spec)
+    sys.modules["wl"] = W          # dataclasses resolve their module through sys.modules
     spec.loader.exec_module(W)
 
     dev = torch.device("cuda", 0)
