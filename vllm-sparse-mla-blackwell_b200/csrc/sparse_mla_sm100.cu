@@ -12,8 +12,9 @@
 // Per CTA (256 threads, one CTA per SM, ~219 KB shared memory)
 //   warps 0-3  softmax + epilogue  (warp w owns TMEM lanes 32w..32w+31)
 //   warps 4-6  gather: bf16 KV by 16-byte cp.async, fp8 KV by register loads
-//              + dequantisation, into a 2-stage ring
-//   warp  7    TMEM allocator + UMMA issuer (one lane, event driven)
+//              + dequantisation, into a 2-stage ring; lane 0 of warp 4 also
+//              issues GEMM2 (below) as soon as a tile's P is written
+//   warp  7    TMEM allocator + GEMM1 issuer (one lane)
 //
 // Index handling: the CTA first compacts its chunk of the index list to the
 // valid entries (order preserved), so masked indices cost neither bandwidth
@@ -29,8 +30,10 @@
 //          N=NH (heads), K=64; A=KV read MN-major from the same smem tile,
 //          B=P K-major; O^T accumulates in TMEM across all tiles. The four
 //          d-chunks are issued interleaved so consecutive UMMAs are independent.
-// The UMMA issuer runs GEMM2(t) as soon as P(t) is ready (it frees a stage)
-// and GEMM1(t+1) as soon as its rows have landed.
+// Two threads issue UMMAs, each in straight-line bursts: GEMM1(t) as soon as
+// tile t's rows have landed, GEMM2(t) as soon as P(t) is written. The tensor
+// pipe interleaves the two streams, so the GEMM2 that frees a stage never
+// waits for a whole GEMM1 burst.
 // The running max only moves when a head's tile max exceeds it by more than
 // 2^8; then the O^T columns of the moved heads are rescaled in TMEM.
 //
@@ -88,14 +91,15 @@ constexpr uint32_t kSmemBytes = kSmUsed + 1024;       // + slack to align the ba
 // mbarrier slots
 enum : int {
   kBarKvFull = 0,    // [2] producers -> MMA: stage loaded
-  kBarKvEmpty = 2,   // [2] MMA (commit) -> producers: stage consumed by GEMM2
-  kBarSFull = 4,     // [2] MMA (commit) -> softmax: S ready
-  kBarSEmpty = 6,    // [2] softmax -> MMA: S buffer read
-  kBarPFull = 8,     // [2] softmax -> MMA: P written (and O rescaled)
-  kBarODone = 10,    // MMA (commit) -> softmax: a GEMM2 finished
-  kBarDrain = 11,    // MMA (commit) -> MMA: every UMMA finished
-  kBarQFull = 12,    // all threads (cp.async) -> MMA: Q landed
-  kNumBars = 13
+  kBarKvEmpty = 2,   // [2] GEMM2 (commit) -> producers: stage consumed by GEMM2
+  kBarSFull = 4,     // [2] GEMM1 (commit) -> softmax: S ready
+  kBarSEmpty = 6,    // [2] softmax -> GEMM1 issuer: S buffer read
+  kBarPFull = 8,     // [2] softmax -> GEMM2 issuer: P written (and O rescaled)
+  kBarODone = 10,    // GEMM2 (commit) -> softmax: a GEMM2 finished
+  kBarDrain = 11,    // GEMM1 issuer's UMMAs all retired
+  kBarQFull = 12,    // all threads (cp.async) -> GEMM1 issuer: Q landed
+  kBarDrain2 = 13,   // GEMM2 issuer's UMMAs all retired
+  kNumBars = 14
 };
 
 // misc words
@@ -183,6 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
     }
     mbar_init(bar(kBarODone), 1);
     mbar_init(bar(kBarDrain), 1);
+    mbar_init(bar(kBarDrain2), 1);
     mbar_init(bar(kBarQFull), kThreads);
     misc[kMiscAbort] = 0;
     fence_mbarrier_init();
@@ -254,10 +259,53 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
   const uint32_t tmem = misc[kMiscTmem];
   const int n_tiles = (n_valid + kRows - 1) / kRows;
 
+  // UMMA steps. GEMM1 of tile t is 32 K-steps into S[t & 1]; GEMM2 of tile t
+  // is 4 K-steps x 4 d-chunks into O^T, chunks innermost so consecutive UMMAs
+  // are independent.
+  constexpr uint32_t kIdesc1 = idesc_bf16_f32(64, 64, false, false);
+  constexpr uint32_t kIdesc2 = idesc_bf16_f32(128, NH, true, false);
+  constexpr int kSteps1 = kDim / 16;          // 32
+  constexpr int kSteps2 = (kRows / 16) * 4;   // 16
+  auto gemm1_step = [=](int t, int kk) {
+    const uint32_t stage = sb + kSmKV + (t & 1) * kStageBytes;
+    const uint32_t off = (kk >> 2) * 8192u + (kk & 3) * 32u;
+    umma_bf16(tmem + kTmemS + 64u * (t & 1), sdesc_sw128(sb + kSmQ + off, 16, 1024),
+              sdesc_sw128(stage + off, 16, 1024), kIdesc1, kk > 0 ? 1u : 0u);
+  };
+  auto gemm2_step = [=](int t, int i) {
+    const int kk = i >> 2, m = i & 3;
+    const uint32_t stage = sb + kSmKV + (t & 1) * kStageBytes;
+    const uint32_t pbuf = sb + kSmP + (t & 1) * kPBytes;
+    umma_bf16(tmem + static_cast<uint32_t>(m * NH),
+              sdesc_sw128(stage + m * 16384u + kk * 2048u, 8192, 1024),
+              sdesc_sw128(pbuf + kk * 32u, 16, 1024), kIdesc2, (t > 0 || kk > 0) ? 1u : 0u);
+  };
+
   // ------------------------------------------------------------------ roles
   if (warp >= kProducerWarp0 && warp < kMmaWarp) {
-    // ================= gather =================
+    // ================= gather + GEMM2 issue =================
+    // Lane 0 of the first gather warp issues GEMM2(t - 2) as soon as P(t - 2)
+    // is written, then every gather thread waits for that GEMM2 to retire
+    // before refilling its stage with tile t. GEMM2 thus never queues behind
+    // a GEMM1 burst of the other issuer (warp 7): the tensor pipe interleaves
+    // the two streams and the stage is recycled as early as possible.
     const int pw = warp - kProducerWarp0;
+    const bool g2_issuer = pw == 0 && lane == 0;
+    auto issue_gemm2 = [&](int t) {
+      if (mbar_wait_bounded(bar(kBarPFull + (t & 1)), (t >> 1) & 1, abort_flag, p.timeout_ns)) {
+        tc_fence_after();
+#pragma unroll
+        for (int i = 0; i < kSteps2; ++i) gemm2_step(t, i);
+      }
+      umma_commit(bar(kBarKvEmpty + (t & 1)));
+      umma_commit(bar(kBarODone));
+    };
+    auto recycle = [&](int t) -> bool {   // stage of tile t is free again
+      if (t < 2) return true;
+      if (g2_issuer) issue_gemm2(t - 2);
+      __syncwarp();
+      return mbar_wait_bounded(bar(kBarKvEmpty + (t & 1)), ((t >> 1) - 1) & 1, abort_flag, p.timeout_ns);
+    };
     if constexpr (!kFp8) {
       // 16-byte cp.async per lane, half a row per warp instruction; the
       // deferred arrive (.noinc) completes the stage once this thread's copies
@@ -265,9 +313,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
       const uint8_t* kvb = static_cast<const uint8_t*>(p.kv);
       for (int t = 0; t < n_tiles; ++t) {
         const int s = t & 1;
-        if (t >= 2 &&
-            !mbar_wait_bounded(bar(kBarKvEmpty + s), ((t >> 1) - 1) & 1, abort_flag, p.timeout_ns))
-          break;
+        if (!recycle(t)) break;
         const uint32_t stage = sb + kSmKV + s * kStageBytes;
         const int rows = min(kRows, n_valid - kRows * t);
 #pragma unroll 4
@@ -287,9 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
       const uint8_t* kv8 = static_cast<const uint8_t*>(p.kv);
       for (int t = 0; t < n_tiles; ++t) {
         const int s = t & 1;
-        if (t >= 2 &&
-            !mbar_wait_bounded(bar(kBarKvEmpty + s), ((t >> 1) - 1) & 1, abort_flag, p.timeout_ns))
-          break;
+        if (!recycle(t)) break;
         const uint32_t stage = sb + kSmKV + s * kStageBytes;
         const int rows = min(kRows, n_valid - kRows * t);
         constexpr int kPer = (kRows + kProducerWarps - 1) / kProducerWarps;
@@ -317,81 +361,32 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
         mbar_arrive(bar(kBarKvFull + s));
       }
     }
+    if (g2_issuer) {
+      // GEMM2 of the last two tiles, then wait until every UMMA this thread
+      // issued has retired (TMEM must not be released under them).
+      for (int t = max(0, n_tiles - 2); t < n_tiles; ++t) issue_gemm2(t);
+      umma_commit(bar(kBarDrain2));
+      int no_abort = 0;
+      mbar_wait_bounded(bar(kBarDrain2), 0, &no_abort, p.timeout_ns);
+    }
     __syncwarp();
   } else if (warp == kMmaWarp) {
-    // ================= UMMA issue =================
+    // ================= GEMM1 issue =================
+    // One straight-line burst of 32 UMMAs per tile. Waits sit only between
+    // bursts: a data-dependent branch inside a burst stalls the issuing
+    // thread for hundreds of cycles per UMMA.
     if (lane == 0) {
-      constexpr uint32_t kIdesc1 = idesc_bf16_f32(64, 64, false, false);
-      constexpr uint32_t kIdesc2 = idesc_bf16_f32(128, NH, true, false);
-      // GEMM1 of tile g1 is 32 K-steps into S; GEMM2 of tile g2 is 4 K-steps
-      // x 4 d-chunks into O^T, chunks innermost so consecutive UMMAs are
-      // independent. Readiness is probed only between issue sequences: a
-      // barrier probe between UMMAs stalls the issuing thread. When both are
-      // ready, the GEMM2 steps are paired with the first 16 GEMM1 steps and
-      // committed at once (freeing the stage early), then GEMM1 finishes.
-      auto gemm1_step = [=](int t, int kk) {
-        const uint32_t stage = sb + kSmKV + (t & 1) * kStageBytes;
-        const uint32_t off = (kk >> 2) * 8192u + (kk & 3) * 32u;
-        umma_bf16(tmem + kTmemS + 64u * (t & 1), sdesc_sw128(sb + kSmQ + off, 16, 1024),
-                  sdesc_sw128(stage + off, 16, 1024), kIdesc1, kk > 0 ? 1u : 0u);
-      };
-      auto gemm2_step = [=](int t, int i) {
-        const int kk = i >> 2, m = i & 3;
-        const uint32_t stage = sb + kSmKV + (t & 1) * kStageBytes;
-        const uint32_t pbuf = sb + kSmP + (t & 1) * kPBytes;
-        umma_bf16(tmem + static_cast<uint32_t>(m * NH),
-                  sdesc_sw128(stage + m * 16384u + kk * 2048u, 8192, 1024),
-                  sdesc_sw128(pbuf + kk * 32u, 16, 1024), kIdesc2, (t > 0 || kk > 0) ? 1u : 0u);
-      };
-      constexpr int kSteps1 = kDim / 16;          // 32
-      constexpr int kSteps2 = (kRows / 16) * 4;   // 16
       bool ok = n_tiles == 0 || mbar_wait_bounded(bar(kBarQFull), 0, abort_flag, p.timeout_ns);
-      fence_proxy_async_smem();   // Q written by cp.async -> tensor-core reads
-      int g1 = 0, g2 = 0;         // next tile for GEMM1 / GEMM2
-      uint64_t t_idle = 0;
-      while (ok && g2 < n_tiles) {
-        const bool ready2 = g2 < g1 && mbar_test_wait(bar(kBarPFull + (g2 & 1)), (g2 >> 1) & 1);
-        const bool ready1 = g1 < n_tiles && g1 < g2 + 2 &&
-                            mbar_test_wait(bar(kBarKvFull + (g1 & 1)), (g1 >> 1) & 1) &&
-                            (g1 < 2 || mbar_test_wait(bar(kBarSEmpty + (g1 & 1)), ((g1 >> 1) - 1) & 1));
-        if (!ready1 && !ready2) {
-          if (*abort_flag) {
-            ok = false;
-          } else {
-            const uint64_t now = global_timer_ns();
-            if (t_idle == 0) {
-              t_idle = now;
-            } else if (now - t_idle > p.timeout_ns) {
-              *abort_flag = 1;
-              ok = false;
-            }
-          }
-          continue;
-        }
-        t_idle = 0;
-        if (ready1) fence_proxy_async_smem();   // generic-proxy smem writes -> tensor-core reads
+      for (int g1 = 0; ok && g1 < n_tiles; ++g1) {
+        ok = mbar_wait_bounded(bar(kBarKvFull + (g1 & 1)), (g1 >> 1) & 1, abort_flag, p.timeout_ns) &&
+             (g1 < 2 ||
+              mbar_wait_bounded(bar(kBarSEmpty + (g1 & 1)), ((g1 >> 1) - 1) & 1, abort_flag, p.timeout_ns));
+        if (!ok) break;
+        fence_proxy_async_smem();   // generic-proxy / cp.async smem writes -> tensor-core reads
         tc_fence_after();
-        if (ready2) {
 #pragma unroll
-          for (int i = 0; i < kSteps2; ++i) {
-            gemm2_step(g2, i);
-            if (ready1) gemm1_step(g1, i);
-          }
-          umma_commit(bar(kBarKvEmpty + (g2 & 1)));
-          umma_commit(bar(kBarODone));
-          ++g2;
-          if (ready1) {
-#pragma unroll
-            for (int i = kSteps2; i < kSteps1; ++i) gemm1_step(g1, i);
-            umma_commit(bar(kBarSFull + (g1 & 1)));
-            ++g1;
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < kSteps1; ++i) gemm1_step(g1, i);
-          umma_commit(bar(kBarSFull + (g1 & 1)));
-          ++g1;
-        }
+        for (int i = 0; i < kSteps1; ++i) gemm1_step(g1, i);
+        umma_commit(bar(kBarSFull + (g1 & 1)));
       }
       // Drain: never release TMEM while a UMMA may still write it.
       umma_commit(bar(kBarDrain));
