@@ -10,10 +10,9 @@
 //   so no global scratch and no second launch are needed.
 //
 // Per CTA (256 threads, one CTA per SM, ~219 KB shared memory)
-//   warps 0-3  softmax + epilogue  (warp w owns TMEM lanes 32w..32w+31)
+//   warps 0-3  softmax, GEMM2 issue, epilogue (warp w owns TMEM lanes 32w..)
 //   warps 4-6  gather: bf16 KV by 16-byte cp.async, fp8 KV by register loads
-//              + dequantisation, into a 2-stage ring; lane 0 of warp 4 also
-//              issues GEMM2 (below) as soon as a tile's P is written
+//              + dequantisation, into a 2-stage ring
 //   warp  7    TMEM allocator + GEMM1 issuer (one lane)
 //
 // Index handling: the CTA first compacts its chunk of the index list to the
@@ -30,9 +29,10 @@
 //          N=NH (heads), K=64; A=KV read MN-major from the same smem tile,
 //          B=P K-major; O^T accumulates in TMEM across all tiles. The four
 //          d-chunks are issued interleaved so consecutive UMMAs are independent.
-// Two threads issue UMMAs, each in straight-line bursts: GEMM1(t) as soon as
-// tile t's rows have landed, GEMM2(t) as soon as P(t) is written. The tensor
-// pipe interleaves the two streams, so the GEMM2 that frees a stage never
+// UMMAs are issued in short straight-line bursts by five threads: warp 7
+// issues GEMM1(t) as soon as tile t's rows have landed; once P(t) is written,
+// each softmax warp issues the 4 K-steps of one d-chunk of GEMM2(t). The
+// tensor pipe interleaves the streams, so the GEMM2 that frees a stage never
 // waits for a whole GEMM1 burst.
 // The running max only moves when a head's tile max exceeds it by more than
 // 2^8; then the O^T columns of the moved heads are rescaled in TMEM.
@@ -91,15 +91,13 @@ constexpr uint32_t kSmemBytes = kSmUsed + 1024;       // + slack to align the ba
 // mbarrier slots
 enum : int {
   kBarKvFull = 0,    // [2] producers -> MMA: stage loaded
-  kBarKvEmpty = 2,   // [2] GEMM2 (commit) -> producers: stage consumed by GEMM2
+  kBarKvEmpty = 2,   // [2] GEMM2 (4 commits) -> producers: stage consumed
   kBarSFull = 4,     // [2] GEMM1 (commit) -> softmax: S ready
   kBarSEmpty = 6,    // [2] softmax -> GEMM1 issuer: S buffer read
-  kBarPFull = 8,     // [2] softmax -> GEMM2 issuer: P written (and O rescaled)
-  kBarODone = 10,    // GEMM2 (commit) -> softmax: a GEMM2 finished
+  kBarODone = 10,    // GEMM2 (4 commits) -> softmax: a GEMM2 finished
   kBarDrain = 11,    // GEMM1 issuer's UMMAs all retired
   kBarQFull = 12,    // all threads (cp.async) -> GEMM1 issuer: Q landed
-  kBarDrain2 = 13,   // GEMM2 issuer's UMMAs all retired
-  kNumBars = 14
+  kNumBars = 13
 };
 
 // misc words
@@ -180,14 +178,12 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
   if (tid == 0) {
     for (int s = 0; s < 2; ++s) {
       mbar_init(bar(kBarKvFull + s), kProducerThreads);
-      mbar_init(bar(kBarKvEmpty + s), 1);
+      mbar_init(bar(kBarKvEmpty + s), 4);
       mbar_init(bar(kBarSFull + s), 1);
       mbar_init(bar(kBarSEmpty + s), 128);
-      mbar_init(bar(kBarPFull + s), 128);
     }
-    mbar_init(bar(kBarODone), 1);
+    mbar_init(bar(kBarODone), 4);
     mbar_init(bar(kBarDrain), 1);
-    mbar_init(bar(kBarDrain2), 1);
     mbar_init(bar(kBarQFull), kThreads);
     misc[kMiscAbort] = 0;
     fence_mbarrier_init();
@@ -265,7 +261,6 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
   constexpr uint32_t kIdesc1 = idesc_bf16_f32(64, 64, false, false);
   constexpr uint32_t kIdesc2 = idesc_bf16_f32(128, NH, true, false);
   constexpr int kSteps1 = kDim / 16;          // 32
-  constexpr int kSteps2 = (kRows / 16) * 4;   // 16
   auto gemm1_step = [=](int t, int kk) {
     const uint32_t stage = sb + kSmKV + (t & 1) * kStageBytes;
     const uint32_t off = (kk >> 2) * 8192u + (kk & 3) * 32u;
@@ -283,28 +278,11 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
 
   // ------------------------------------------------------------------ roles
   if (warp >= kProducerWarp0 && warp < kMmaWarp) {
-    // ================= gather + GEMM2 issue =================
-    // Lane 0 of the first gather warp issues GEMM2(t - 2) as soon as P(t - 2)
-    // is written, then every gather thread waits for that GEMM2 to retire
-    // before refilling its stage with tile t. GEMM2 thus never queues behind
-    // a GEMM1 burst of the other issuer (warp 7): the tensor pipe interleaves
-    // the two streams and the stage is recycled as early as possible.
+    // ================= gather =================
     const int pw = warp - kProducerWarp0;
-    const bool g2_issuer = pw == 0 && lane == 0;
-    auto issue_gemm2 = [&](int t) {
-      if (mbar_wait_bounded(bar(kBarPFull + (t & 1)), (t >> 1) & 1, abort_flag, p.timeout_ns)) {
-        tc_fence_after();
-#pragma unroll
-        for (int i = 0; i < kSteps2; ++i) gemm2_step(t, i);
-      }
-      umma_commit(bar(kBarKvEmpty + (t & 1)));
-      umma_commit(bar(kBarODone));
-    };
     auto recycle = [&](int t) -> bool {   // stage of tile t is free again
-      if (t < 2) return true;
-      if (g2_issuer) issue_gemm2(t - 2);
-      __syncwarp();
-      return mbar_wait_bounded(bar(kBarKvEmpty + (t & 1)), ((t >> 1) - 1) & 1, abort_flag, p.timeout_ns);
+      return t < 2 ||
+             mbar_wait_bounded(bar(kBarKvEmpty + (t & 1)), ((t >> 1) - 1) & 1, abort_flag, p.timeout_ns);
     };
     if constexpr (!kFp8) {
       // 16-byte cp.async per lane, half a row per warp instruction; the
@@ -360,14 +338,6 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
         fence_proxy_async_smem();
         mbar_arrive(bar(kBarKvFull + s));
       }
-    }
-    if (g2_issuer) {
-      // GEMM2 of the last two tiles, then wait until every UMMA this thread
-      // issued has retired (TMEM must not be released under them).
-      for (int t = max(0, n_tiles - 2); t < n_tiles; ++t) issue_gemm2(t);
-      umma_commit(bar(kBarDrain2));
-      int no_abort = 0;
-      mbar_wait_bounded(bar(kBarDrain2), 0, &no_abort, p.timeout_ns);
     }
     __syncwarp();
   } else if (warp == kMmaWarp) {
@@ -488,8 +458,18 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
         }
         fence_proxy_async_smem();
       }
+      // GEMM2(t) right away: once every P row is written (and O rescaled),
+      // lane 0 of each softmax warp issues the 4 K-steps of d-chunk `warp`.
       tc_fence_before();
-      mbar_arrive(bar(kBarPFull + b));
+      named_bar_sync(2, 128);
+      if (lane == 0) {
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) gemm2_step(t, 4 * kk + warp);
+        umma_commit(bar(kBarKvEmpty + b));
+        umma_commit(bar(kBarODone));
+      }
+      __syncwarp();
     }
 
     // publish this CTA's per-head max and sum for the merge
