@@ -32,7 +32,8 @@ enum glm53_status {
   GLM53_ERR_ALIGN = 6,         /* a pointer is null or not 16-byte aligned       */
   GLM53_ERR_SPLITS = 7,        /* explicit split count not in {0, 1, 2, 4, 8}    */
   GLM53_ERR_CUDA = 8,          /* a CUDA runtime call failed                     */
-  GLM53_ERR_DEVICE = 9         /* current device is not sm_100                   */
+  GLM53_ERR_DEVICE = 9,        /* current device is not sm_100                   */
+  GLM53_ERR_WORKSPACE = 10     /* workspace missing, misaligned or too small     */
 };
 
 /* KV pool element type. */
@@ -77,6 +78,36 @@ int glm53_sparse_mla_fwd(const void* q, const void* kv, const int32_t* indices, 
                          float* lse, int64_t T, int64_t H, int64_t head_dim, int64_t kv_rows,
                          int64_t kv_width, int64_t topk, int kv_dtype, float sm_scale,
                          float kv_scale, int splits, void* stream);
+
+/*
+ * Bytes of global workspace glm53_sparse_mla_fwd_ws needs for this shape on
+ * the current device (0 when each token runs on a single CTA). Resolves
+ * splits == 0 exactly as the forward does. The size is
+ * T * splits * (Hp * 512 + 2 * Hp) * 4 bytes, Hp = max(H, 16): 16 MiB for a
+ * 32-token, 64-head decode batch split 4 ways.
+ * No counterpart in the reference, whose kernel never splits a token.
+ */
+int glm53_sparse_mla_workspace_bytes(int64_t T, int64_t H, int64_t topk, int splits,
+                                     uint64_t* bytes);
+
+/*
+ * As glm53_sparse_mla_fwd, with the per-token split partials merged through
+ * `workspace` (global memory, 16-byte aligned, at least
+ * glm53_sparse_mla_workspace_bytes; unused when no token is split) instead of
+ * distributed shared memory. All 8 warps of a CTA take part and the traffic
+ * stays in L2, which makes the merge of small decode batches several times
+ * cheaper. Every byte the kernel reads from the workspace it first writes in
+ * the same launch, so it needs no initialisation, but two launches that may
+ * run concurrently must not share one workspace.
+ * Replaces the same host launcher as glm53_sparse_mla_fwd
+ * (csrc/sparse_mla.cu:434-498); this is what the torch op calls, with the
+ * workspace taken from the PyTorch caching allocator.
+ */
+int glm53_sparse_mla_fwd_ws(const void* q, const void* kv, const int32_t* indices, void* out,
+                            float* lse, int64_t T, int64_t H, int64_t head_dim, int64_t kv_rows,
+                            int64_t kv_width, int64_t topk, int kv_dtype, float sm_scale,
+                            float kv_scale, int splits, void* workspace,
+                            uint64_t workspace_bytes, void* stream);
 
 /*
  * Argument validation alone, with no CUDA call: returns the status that

@@ -77,8 +77,26 @@ def test_fwd_rejects_before_touching_cuda(lib):
     # null / misaligned pointers
     assert f(None, None, None, None, None, 4, 64, 512, 64, 512, 64, 0, 0.1, 1.0, 0, None) == E_ALIGN
     assert f(16, 32, 48, 65, None, 4, 64, 512, 64, 512, 64, 0, 0.1, 1.0, 0, None) == E_ALIGN
-    for code in range(10):
+    for code in range(11):
         assert lib.glm53_sparse_mla_strerror(code)
+
+
+def test_workspace_entry_points_validate_before_cuda(lib):
+    import ctypes
+    nb = ctypes.c_uint64(7)
+    wsb = lib.glm53_sparse_mla_workspace_bytes
+    wsb.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int,
+                    ctypes.POINTER(ctypes.c_uint64)]
+    assert wsb(4, 12, 2048, 0, ctypes.byref(nb)) == E_HEADS
+    assert wsb(0, 64, 2048, 0, ctypes.byref(nb)) == OK and nb.value == 0
+    f = lib.glm53_sparse_mla_fwd_ws
+    f.argtypes = [ctypes.c_void_p] * 5 + [ctypes.c_int64] * 6 + [
+        ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_int, ctypes.c_void_p,
+        ctypes.c_uint64, ctypes.c_void_p]
+    assert f(None, None, None, None, None, 4, 12, 512, 64, 512, 64, 0, 0.1, 1.0, 0, None, 0,
+             None) == E_HEADS
+    assert f(None, None, None, None, None, 0, 64, 512, 64, 512, 64, 0, 0.1, 1.0, 0, None, 0,
+             None) == OK
 
 
 def test_auto_splits(lib):

@@ -235,3 +235,75 @@ def test_no_timeouts_recorded():
     torch.cuda.synchronize()
     assert lib.glm53_sparse_mla_device_status(ctypes.byref(st), 1) == 0
     assert st.value & 1 == 0, "a pipeline wait timed out"
+
+
+def _abi_ws():
+    lib = ctypes.CDLL(G.library_path())
+    lib.glm53_sparse_mla_fwd_ws.restype = ctypes.c_int
+    lib.glm53_sparse_mla_fwd_ws.argtypes = [
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+        ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+        ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_int,
+        ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p]
+    lib.glm53_sparse_mla_workspace_bytes.restype = ctypes.c_int
+    lib.glm53_sparse_mla_workspace_bytes.argtypes = [
+        ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.POINTER(ctypes.c_uint64)]
+    return lib
+
+
+def abi_fwd_ws(lib, w: W.Workload, splits: int, lse=None, ws_bytes=None, poison=True):
+    nb = ctypes.c_uint64(0)
+    assert lib.glm53_sparse_mla_workspace_bytes(w.T, w.H, w.topk, splits, ctypes.byref(nb)) == 0
+    size = nb.value if ws_bytes is None else ws_bytes
+    # 0xFF bytes are NaNs: the merge must not read anything it did not write
+    ws = torch.full((max(size, 16),), 0xFF if poison else 0, dtype=torch.uint8, device="cuda")
+    out = torch.full_like(w.q, float("nan"))
+    kvd = 1 if w.kv.dtype == torch.float8_e4m3fn else 0
+    rc = lib.glm53_sparse_mla_fwd_ws(
+        w.q.data_ptr(), w.kv.data_ptr(), w.indices.data_ptr(), out.data_ptr(),
+        lse.data_ptr() if lse is not None else None, w.T, w.H, 512, w.kv.shape[0], 512, w.topk,
+        kvd, w.sm_scale, w.kv_scale, splits, ws.data_ptr() if size else None, size,
+        torch.cuda.current_stream().cuda_stream)
+    return rc, out, nb.value
+
+
+@pytest.mark.parametrize("splits", [2, 4, 8])
+@pytest.mark.parametrize("heads", [64, 32, 16, 8])
+def test_c_abi_workspace_merge(splits, heads):
+    """The L2-workspace split merge (all 8 warps) on the whole case matrix,
+    with the LSE output, the workspace pre-filled with NaN bytes."""
+    lib = _abi_ws()
+    for w in W.case_matrix(heads=heads, topk=2048, rows=8192, device="cuda"):
+        lse = torch.empty(w.T, w.H, device="cuda")
+        rc, out, nbytes = abi_fwd_ws(lib, w, splits, lse)
+        assert rc == 0 and nbytes > 0, (rc, nbytes)
+        torch.cuda.synchronize()
+        ref, ref_lse = _oracle(w)
+        _check(f"{w.name}/ws/s{splits}", out, ref, w.indices)
+        got = lse.cpu().numpy()
+        fin = np.isfinite(ref_lse)
+        assert np.array_equal(np.isneginf(got), np.isneginf(ref_lse))
+        if fin.any():
+            err = np.abs(got[fin] - ref_lse[fin]).max()
+            assert err <= LSE_TOL * max(1.0, np.abs(ref_lse[fin]).max() / 100), (w.name, err)
+
+
+def test_workspace_contract():
+    """Size formula, the missing / short workspace error, and a single-CTA
+    split that needs none."""
+    lib = _abi_ws()
+    w = W.config_c2(device="cuda")
+    nb = ctypes.c_uint64(0)
+    assert lib.glm53_sparse_mla_workspace_bytes(w.T, w.H, w.topk, 4, ctypes.byref(nb)) == 0
+    assert nb.value == w.T * 4 * (64 * 512 + 2 * 64) * 4
+    assert lib.glm53_sparse_mla_workspace_bytes(w.T, w.H, w.topk, 1, ctypes.byref(nb)) == 0
+    assert nb.value == 0
+    rc, _, need = abi_fwd_ws(lib, w, 4, ws_bytes=0)
+    assert rc == 10, rc                       # GLM53_ERR_WORKSPACE: none given
+    rc, _, _ = abi_fwd_ws(lib, w, 4, ws_bytes=need - 16)
+    assert rc == 10, rc                       # one float4 short
+    rc, out, _ = abi_fwd_ws(lib, w, 1, ws_bytes=0)
+    assert rc == 0
+    torch.cuda.synchronize()
+    ref, _ = _oracle(w)
+    _check("c2/ws/s1", out, ref, w.indices)

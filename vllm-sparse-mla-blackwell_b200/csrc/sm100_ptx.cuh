@@ -148,6 +148,33 @@ __device__ __forceinline__ void stg_v4(void* p, uint4 v) {
                : "memory");
 }
 
+// 16-byte global store / load cached in L2 only (.cg): for data that other
+// CTAs of the same launch exchange through a workspace, never through L1.
+__device__ __forceinline__ void stg_cg_f4(void* p, float4 v) {
+  asm volatile("st.global.cg.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w)
+               : "memory");
+}
+
+__device__ __forceinline__ float4 ldg_cg_f4(const void* p) {
+  float4 v;
+  asm volatile("ld.global.cg.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void stg_cg_f32(float* p, float v) {
+  asm volatile("st.global.cg.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
+}
+
+__device__ __forceinline__ float ldg_cg_f32(const float* p) {
+  float v;
+  asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // Order this thread's generic-proxy shared-memory accesses before later
 // async-proxy (tensor core) accesses.
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -109,6 +109,7 @@ struct Params {
   const int32_t* idx;       // [T, topk]
   __nv_bfloat16* out;       // [T, H, 512]
   float* lse;               // [T, H] or nullptr
+  float* ws;                // split-merge workspace (see the merge), or nullptr
   long long kv_rows;
   int T, H, topk, splits, chunk;
   float c;                  // sm_scale * log2(e)
@@ -148,6 +149,22 @@ __device__ __forceinline__ void dequant16(const uint4 w, float scale, uint4& lo,
   hi.y = dequant2(w.z >> 16, scale);
   hi.z = dequant2(w.w & 0xFFFFu, scale);
   hi.w = dequant2(w.w >> 16, scale);
+}
+
+// bf16 store of out[h0 + j][d] for j < N: neighbouring lanes (d, d ^ 1) swap
+// one value per head pair so each lane writes a bf16x2 of two adjacent d.
+template <int N>
+__device__ __forceinline__ void store_pairs_n(__nv_bfloat16* o_tok, int H, int d, int h0,
+                                              const float (&o)[N]) {
+  const bool odd = threadIdx.x & 1;
+  const int d_even = d & ~1;
+#pragma unroll
+  for (int j = 0; j < N; j += 2) {
+    const float recv = __shfl_xor_sync(0xFFFFFFFFu, odd ? o[j] : o[j + 1], 1);
+    const int hw = h0 + (odd ? j + 1 : j);
+    const uint32_t pair = odd ? pack_bf16x2(recv, o[j + 1]) : pack_bf16x2(o[j], recv);
+    if (hw < H) *reinterpret_cast<uint32_t*>(o_tok + static_cast<size_t>(hw) * kDim + d_even) = pair;
+  }
 }
 
 template <int NH, bool kFp8>
@@ -516,7 +533,128 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
     }
   };
 
-  if (nranks == 1) {
+  if (nranks > 1 && p.ws != nullptr) {
+    // ---- split across 2, 4 or 8 CTAs, merged through a global workspace
+    // (it stays in L2). Each CTA owns a d-slice of the output. All 8 warps
+    // work: warp w reads TMEM lane quadrant w & 3 and head half w >> 2 (at
+    // NH = 16, warps 0-3 take all heads). Workspace per (token, CTA): m[NH],
+    // l[NH], then one slice per destination CTA laid out [NH / 4][dspan][4]
+    // floats, so a warp's 16-byte stores and loads cover 512 contiguous bytes.
+    // Every slice is written before the cluster barrier and read after it,
+    // so the workspace needs no initialisation.
+    constexpr int kHalf = NH >= 32 ? NH / 2 : NH;
+    const int dspan = kDim / nranks;
+    const size_t blk = static_cast<size_t>(NH) * kDim + 2 * NH;   // floats per (token, CTA)
+    float* const ws_tok = p.ws + static_cast<size_t>(token) * nranks * blk;
+    float* const ws_me = ws_tok + static_cast<size_t>(split) * blk;
+    const int qd = warp & 3;
+    const bool active = NH >= 32 || warp < 4;
+    const int h0 = NH >= 32 ? (warp >> 2) * kHalf : 0;
+    const uint32_t tcol = static_cast<uint32_t>(32 * qd) << 16;
+    float* const scal = reinterpret_cast<float*>(gb + kSmIdx);   // e[8][NH], 1/L[NH]
+    auto load_half = [=](int m, float (&o)[kHalf]) {
+      const uint32_t ta = tmem + tcol + static_cast<uint32_t>(m * NH + h0);
+      if constexpr (kHalf == 32) {
+        tmem_ld_32x32b_x32(ta, o);
+      } else {
+        tmem_ld_32x32b_x16(ta, o);
+      }
+      tmem_wait_ld();
+    };
+
+    if (n_tiles > 0) mbar_wait_bounded(bar(kBarODone), (n_tiles - 1) & 1, abort_flag, p.timeout_ns);
+    __syncthreads();   // every role past its main loop; m_sm / l_sm written
+    tc_fence_after();
+    if (tid < NH) {
+      stg_cg_f32(ws_me + tid, m_sm[tid]);
+      stg_cg_f32(ws_me + NH + tid, l_sm[tid]);
+    }
+    if (active) {
+#pragma unroll 1
+      for (int m = 0; m < 4; ++m) {
+        const int d = 128 * m + 32 * qd + lane;
+        const int owner = d / dspan;               // warp-uniform (dspan >= 64)
+        if (owner == split) continue;
+        float o[kHalf];
+        load_half(m, o);
+        if (n_tiles == 0) {
+#pragma unroll
+          for (int j = 0; j < kHalf; ++j) o[j] = 0.f;
+        }
+        float* const dst = ws_me + 2 * NH + static_cast<size_t>(owner) * NH * dspan;
+        const int dl = d - owner * dspan;
+#pragma unroll
+        for (int c = 0; c < kHalf / 4; ++c)
+          stg_cg_f4(dst + (static_cast<size_t>(h0 / 4 + c) * dspan + dl) * 4,
+                    make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]));
+      }
+    }
+    __threadfence();
+    cluster_sync_all();   // every CTA's workspace stores visible cluster-wide
+    if (tid < NH) {
+      float mr[8], lr[8];
+      float M = -INFINITY;
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        if (r < nranks) {
+          if (r == split) {
+            mr[r] = m_sm[tid];
+            lr[r] = l_sm[tid];
+          } else {
+            mr[r] = ldg_cg_f32(ws_tok + r * blk + tid);
+            lr[r] = ldg_cg_f32(ws_tok + r * blk + NH + tid);
+          }
+          if (lr[r] > 0.f) M = fmaxf(M, mr[r]);
+        }
+      }
+      float L = 0.f;
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        if (r < nranks) {
+          const float e = lr[r] > 0.f ? exp2f(mr[r] - M) : 0.f;
+          scal[r * NH + tid] = e;
+          L += lr[r] * e;
+        }
+      }
+      scal[8 * NH + tid] = L > 0.f ? 1.f / L : 0.f;
+      if (split == 0 && p.lse != nullptr && tid < p.H)
+        p.lse[static_cast<size_t>(token) * p.H + tid] = L > 0.f ? log2f(L) + M : -INFINITY;
+    }
+    __syncthreads();
+    if (active) {
+#pragma unroll 1
+      for (int m = 0; m < 4; ++m) {
+        const int d = 128 * m + 32 * qd + lane;
+        if (d / dspan != split) continue;          // warp-uniform
+        const int dl = d - split * dspan;
+        float o[kHalf];
+        load_half(m, o);
+#pragma unroll
+        for (int j = 0; j < kHalf; ++j) o[j] = n_tiles > 0 ? o[j] * scal[split * NH + h0 + j] : 0.f;
+        for (int r = 0; r < nranks; ++r) {
+          if (r == split) continue;
+          const float* src = ws_tok + r * blk + 2 * NH + static_cast<size_t>(split) * NH * dspan;
+          float4 v[kHalf / 4];
+#pragma unroll
+          for (int c = 0; c < kHalf / 4; ++c)
+            v[c] = ldg_cg_f4(src + (static_cast<size_t>(h0 / 4 + c) * dspan + dl) * 4);
+#pragma unroll
+          for (int c = 0; c < kHalf / 4; ++c) {
+            const float* e = scal + r * NH + h0 + 4 * c;
+            o[4 * c] += v[c].x * e[0];
+            o[4 * c + 1] += v[c].y * e[1];
+            o[4 * c + 2] += v[c].z * e[2];
+            o[4 * c + 3] += v[c].w * e[3];
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < kHalf; ++j) o[j] *= scal[8 * NH + h0 + j];
+        store_pairs_n<kHalf>(o_tok, p.H, d, h0, o);
+      }
+    }
+    tc_fence_before();
+    __syncthreads();
+  } else if (nranks == 1) {
     // ---- single CTA per token: normalise and store straight from TMEM
     __syncthreads();
     if (warp < 4) {
@@ -879,10 +1017,29 @@ extern "C" int glm53_sparse_mla_auto_splits(int64_t T, int64_t topk, int sm_coun
 
 extern "C" int glm53_sparse_mla_prepare(void) { return prepare_current_device(nullptr); }
 
-extern "C" int glm53_sparse_mla_fwd(const void* q, const void* kv, const int32_t* indices,
-                                    void* out, float* lse, int64_t T, int64_t H, int64_t head_dim,
-                                    int64_t kv_rows, int64_t kv_width, int64_t topk, int kv_dtype,
-                                    float sm_scale, float kv_scale, int splits, void* stream) {
+namespace glm53 {
+
+int padded_heads(int64_t H) { return H <= 16 ? 16 : static_cast<int>(H); }
+
+// Split count the launcher uses for this shape on device `dev`.
+int resolve_splits(int64_t T, int64_t topk, int splits, int dev) {
+  if (splits != 0) return splits;
+  return g_env_splits > 0 ? g_env_splits : glm53_sparse_mla_auto_splits(T, topk, g_sm_count[dev]);
+}
+
+uint64_t workspace_floats(int64_t T, int64_t H, int splits) {
+  if (splits <= 1) return 0;
+  const uint64_t nh = static_cast<uint64_t>(padded_heads(H));
+  return static_cast<uint64_t>(T) * static_cast<uint64_t>(splits) * (nh * kDim + 2 * nh);
+}
+
+// Shared body of the forward entry points. `ws == nullptr` selects the
+// distributed-shared-memory split merge; otherwise `ws` (at least
+// `ws_bytes`) is the global workspace of the L2 split merge.
+int launch_forward(const void* q, const void* kv, const int32_t* indices, void* out, float* lse,
+                   int64_t T, int64_t H, int64_t head_dim, int64_t kv_rows, int64_t kv_width,
+                   int64_t topk, int kv_dtype, float sm_scale, float kv_scale, int splits,
+                   bool use_ws, void* ws, uint64_t ws_bytes, void* stream) {
   int rc = glm53_sparse_mla_check(T, H, head_dim, kv_rows, kv_width, topk, kv_dtype, splits);
   if (rc != GLM53_OK) return rc;
   if (T == 0) return GLM53_OK;
@@ -893,9 +1050,14 @@ extern "C" int glm53_sparse_mla_fwd(const void* q, const void* kv, const int32_t
   int dev = 0;
   rc = prepare_current_device(&dev);
   if (rc != GLM53_OK) return rc;
-  int s = splits;
-  if (s == 0) s = g_env_splits > 0 ? g_env_splits : glm53_sparse_mla_auto_splits(T, topk, g_sm_count[dev]);
+  const int s = resolve_splits(T, topk, splits, dev);
   if ((topk + s - 1) / s > kMaxChunk) return GLM53_ERR_TOPK;
+  float* wsf = nullptr;
+  if (use_ws && s > 1) {
+    const uint64_t need = 4 * workspace_floats(T, H, s);
+    if (ws == nullptr || !aligned16(ws) || ws_bytes < need) return GLM53_ERR_WORKSPACE;
+    wsf = static_cast<float*>(ws);
+  }
 
   Params p;
   p.q = static_cast<const __nv_bfloat16*>(q);
@@ -903,6 +1065,7 @@ extern "C" int glm53_sparse_mla_fwd(const void* q, const void* kv, const int32_t
   p.idx = indices;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.lse = lse;
+  p.ws = wsf;
   p.kv_rows = kv_rows;
   p.T = static_cast<int>(T);
   p.H = static_cast<int>(H);
@@ -923,6 +1086,41 @@ extern "C" int glm53_sparse_mla_fwd(const void* q, const void* kv, const int32_t
   else
     e = fp8 ? launch_fwd<64, true>(p, s, st) : launch_fwd<64, false>(p, s, st);
   return e == cudaSuccess ? GLM53_OK : GLM53_ERR_CUDA;
+}
+
+}  // namespace glm53
+
+extern "C" int glm53_sparse_mla_fwd(const void* q, const void* kv, const int32_t* indices,
+                                    void* out, float* lse, int64_t T, int64_t H, int64_t head_dim,
+                                    int64_t kv_rows, int64_t kv_width, int64_t topk, int kv_dtype,
+                                    float sm_scale, float kv_scale, int splits, void* stream) {
+  return launch_forward(q, kv, indices, out, lse, T, H, head_dim, kv_rows, kv_width, topk,
+                        kv_dtype, sm_scale, kv_scale, splits, false, nullptr, 0, stream);
+}
+
+extern "C" int glm53_sparse_mla_workspace_bytes(int64_t T, int64_t H, int64_t topk, int splits,
+                                                uint64_t* bytes) {
+  if (bytes == nullptr) return GLM53_ERR_ALIGN;
+  *bytes = 0;
+  const int rc0 = glm53_sparse_mla_check(T, H, kDim, 0, kDim, topk, GLM53_KV_BF16, splits);
+  if (rc0 != GLM53_OK) return rc0;
+  if (T == 0) return GLM53_OK;
+  int dev = 0;
+  const int rc = prepare_current_device(&dev);
+  if (rc != GLM53_OK) return rc;
+  *bytes = 4 * workspace_floats(T, H, resolve_splits(T, topk, splits, dev));
+  return GLM53_OK;
+}
+
+extern "C" int glm53_sparse_mla_fwd_ws(const void* q, const void* kv, const int32_t* indices,
+                                       void* out, float* lse, int64_t T, int64_t H,
+                                       int64_t head_dim, int64_t kv_rows, int64_t kv_width,
+                                       int64_t topk, int kv_dtype, float sm_scale, float kv_scale,
+                                       int splits, void* workspace, uint64_t workspace_bytes,
+                                       void* stream) {
+  return launch_forward(q, kv, indices, out, lse, T, H, head_dim, kv_rows, kv_width, topk,
+                        kv_dtype, sm_scale, kv_scale, splits, true, workspace, workspace_bytes,
+                        stream);
 }
 
 extern "C" int glm53_sparse_mla_device_status(uint32_t* status, int clear) {
@@ -963,6 +1161,7 @@ extern "C" const char* glm53_sparse_mla_strerror(int code) {
     case GLM53_ERR_SPLITS: return "splits must be 0 (auto), 1, 2, 4 or 8";
     case GLM53_ERR_CUDA: return "CUDA runtime error while launching the sparse-MLA kernel";
     case GLM53_ERR_DEVICE: return "the current device is not an sm_100 (B200-class) GPU";
+    case GLM53_ERR_WORKSPACE: return "workspace missing, not 16-byte aligned or smaller than glm53_sparse_mla_workspace_bytes";
     default: return "unknown glm53_sparse_mla status";
   }
 }

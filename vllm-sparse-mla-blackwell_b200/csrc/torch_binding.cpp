@@ -7,7 +7,7 @@
 // Argument checks mirror the reference host op (csrc/sparse_mla.cu:455-498):
 // same conditions, same order (T == 0 returns before the dtype / head-count
 // dispatch), raised as RuntimeError through TORCH_CHECK. The launch itself goes
-// through glm53_sparse_mla_fwd on the caller's current CUDA stream.
+// through glm53_sparse_mla_fwd_ws on the caller's current CUDA stream.
 
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
@@ -54,11 +54,21 @@ void run_sparse_fwd(const torch::Tensor& q, const torch::Tensor& kv, const torch
 
   const c10::cuda::CUDAGuard guard(q.device());
   cudaStream_t stream = c10::cuda::getCurrentCUDAStream(q.get_device()).stream();
-  const int rc = glm53_sparse_mla_fwd(q.data_ptr(), kv.data_ptr(), indices.data_ptr<int32_t>(),
-                                      out.data_ptr(), lse, T, H, q.size(2), kv.size(0),
-                                      kv.size(1), topk, kv_dtype, static_cast<float>(sm_scale),
-                                      static_cast<float>(kv_scale), /*splits=*/0,
-                                      static_cast<void*>(stream));
+  // Split-merge workspace from the caching allocator (stream-ordered, so it
+  // is also valid inside a CUDA graph capture); empty when no token is split.
+  uint64_t ws_bytes = 0;
+  int rc = glm53_sparse_mla_workspace_bytes(T, H, topk, /*splits=*/0, &ws_bytes);
+  TORCH_CHECK(rc == GLM53_OK, "glm53_sparse_mla: ", glm53_sparse_mla_strerror(rc));
+  torch::Tensor ws;
+  if (ws_bytes > 0)
+    ws = torch::empty({static_cast<int64_t>(ws_bytes)},
+                      torch::TensorOptions().dtype(torch::kUInt8).device(q.device()));
+  rc = glm53_sparse_mla_fwd_ws(q.data_ptr(), kv.data_ptr(), indices.data_ptr<int32_t>(),
+                               out.data_ptr(), lse, T, H, q.size(2), kv.size(0), kv.size(1), topk,
+                               kv_dtype, static_cast<float>(sm_scale),
+                               static_cast<float>(kv_scale), /*splits=*/0,
+                               ws_bytes > 0 ? ws.data_ptr() : nullptr, ws_bytes,
+                               static_cast<void*>(stream));
   TORCH_CHECK(rc == GLM53_OK, "glm53_sparse_mla: ", glm53_sparse_mla_strerror(rc));
 }
 
