@@ -33,7 +33,8 @@ enum glm53_status {
   GLM53_ERR_SPLITS = 7,        /* explicit split count not in {0, 1, 2, 4, 8}    */
   GLM53_ERR_CUDA = 8,          /* a CUDA runtime call failed                     */
   GLM53_ERR_DEVICE = 9,        /* current device is not sm_100                   */
-  GLM53_ERR_WORKSPACE = 10     /* workspace missing, misaligned or too small     */
+  GLM53_ERR_WORKSPACE = 10,    /* workspace missing, misaligned or too small     */
+  GLM53_ERR_SCRATCH_LIMIT = 11 /* shape needs more than the no-alloc scratch     */
 };
 
 /* KV pool element type. */
@@ -108,6 +109,30 @@ int glm53_sparse_mla_fwd_ws(const void* q, const void* kv, const int32_t* indice
                             int64_t kv_width, int64_t topk, int kv_dtype, float sm_scale,
                             float kv_scale, int splits, void* workspace,
                             uint64_t workspace_bytes, void* stream);
+
+/*
+ * As glm53_sparse_mla_fwd_ws, for callers that cannot allocate device memory
+ * when they call attention (a fixed-size memory pool, an allocator that the
+ * call site cannot reach, a runtime that forbids cudaMalloc after start-up):
+ * the split-merge workspace is a 32 MiB array built into the library, which
+ * every device that loads the library holds until the process exits. This
+ * call allocates nothing. A shape whose workspace
+ * (glm53_sparse_mla_workspace_bytes) exceeds 32 MiB is rejected with
+ * GLM53_ERR_SCRATCH_LIMIT before any launch. With automatic splitting a
+ * launch that splits its tokens has at most one CTA per SM (148 on B200),
+ * which needs at most 18.6 MiB.
+ * The first call on each device looks up the array's device address (and
+ * sets the kernels' shared-memory limit); make that first call before any
+ * stream capture. All calls share the one array and it keeps the previous
+ * call's contents; the kernel writes every scratch byte it reads within the
+ * same launch, so nothing needs clearing, but calls that can overlap on the
+ * GPU (different streams, or several host threads) race on it.
+ * No counterpart in the reference, which has no split merge and no scratch.
+ */
+int glm53_sparse_mla_fwd_noalloc(const void* q, const void* kv, const int32_t* indices, void* out,
+                                 float* lse, int64_t T, int64_t H, int64_t head_dim,
+                                 int64_t kv_rows, int64_t kv_width, int64_t topk, int kv_dtype,
+                                 float sm_scale, float kv_scale, int splits, void* stream);
 
 /*
  * Argument validation alone, with no CUDA call: returns the status that

@@ -77,7 +77,7 @@ def test_fwd_rejects_before_touching_cuda(lib):
     # null / misaligned pointers
     assert f(None, None, None, None, None, 4, 64, 512, 64, 512, 64, 0, 0.1, 1.0, 0, None) == E_ALIGN
     assert f(16, 32, 48, 65, None, 4, 64, 512, 64, 512, 64, 0, 0.1, 1.0, 0, None) == E_ALIGN
-    for code in range(11):
+    for code in range(12):
         assert lib.glm53_sparse_mla_strerror(code)
 
 

@@ -1123,6 +1123,52 @@ extern "C" int glm53_sparse_mla_fwd_ws(const void* q, const void* kv, const int3
                         stream);
 }
 
+// ---------------------------------------------------------------------------
+// No-allocation entry point
+// ---------------------------------------------------------------------------
+// Some callers cannot allocate device memory at call time: code running
+// under a custom or fixed-size memory pool, embedders whose allocator is not
+// reachable from the attention call site, runtimes that forbid cudaMalloc once
+// serving has started. For them the split-merge workspace is a file-scope
+// device array of a fixed size. Every device that loads this library keeps it
+// (kNoAllocScratchBytes) until the process exits.
+namespace glm53 {
+constexpr uint64_t kNoAllocScratchBytes = 32ull << 20;   // 32 MiB
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / 4];
+void* g_noalloc_addr[kMaxDevices] = {};
+}  // namespace glm53
+
+extern "C" int glm53_sparse_mla_fwd_noalloc(const void* q, const void* kv, const int32_t* indices,
+                                            void* out, float* lse, int64_t T, int64_t H,
+                                            int64_t head_dim, int64_t kv_rows, int64_t kv_width,
+                                            int64_t topk, int kv_dtype, float sm_scale,
+                                            float kv_scale, int splits, void* stream) {
+  int rc = glm53_sparse_mla_check(T, H, head_dim, kv_rows, kv_width, topk, kv_dtype, splits);
+  if (rc != GLM53_OK) return rc;
+  if (T == 0) return GLM53_OK;
+  int dev = 0;
+  rc = prepare_current_device(&dev);
+  if (rc != GLM53_OK) return rc;
+  void* scratch = nullptr;
+  {
+    // The array's host-side name is only a stand-in; its device address is
+    // looked up once per device, with that device current.
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (g_noalloc_addr[dev] == nullptr) {
+      void* ptr = nullptr;
+      if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr)
+        return GLM53_ERR_CUDA;
+      g_noalloc_addr[dev] = ptr;
+    }
+    scratch = g_noalloc_addr[dev];
+  }
+  const int s = resolve_splits(T, topk, splits, dev);
+  if (4 * workspace_floats(T, H, s) > kNoAllocScratchBytes) return GLM53_ERR_SCRATCH_LIMIT;
+  return launch_forward(q, kv, indices, out, lse, T, H, head_dim, kv_rows, kv_width, topk,
+                        kv_dtype, sm_scale, kv_scale, splits, true, scratch, kNoAllocScratchBytes,
+                        stream);
+}
+
 extern "C" int glm53_sparse_mla_device_status(uint32_t* status, int clear) {
   unsigned int v = 0;
   if (cudaMemcpyFromSymbol(&v, g_device_status, sizeof(v)) != cudaSuccess) return GLM53_ERR_CUDA;
@@ -1162,6 +1208,7 @@ extern "C" const char* glm53_sparse_mla_strerror(int code) {
     case GLM53_ERR_CUDA: return "CUDA runtime error while launching the sparse-MLA kernel";
     case GLM53_ERR_DEVICE: return "the current device is not an sm_100 (B200-class) GPU";
     case GLM53_ERR_WORKSPACE: return "workspace missing, not 16-byte aligned or smaller than glm53_sparse_mla_workspace_bytes";
+    case GLM53_ERR_SCRATCH_LIMIT: return "shape needs more split-merge scratch than the 32 MiB built into glm53_sparse_mla_fwd_noalloc; use glm53_sparse_mla_fwd_ws";
     default: return "unknown glm53_sparse_mla status";
   }
 }
