@@ -84,8 +84,8 @@ int glm53_sparse_mla_fwd(const void* q, const void* kv, const int32_t* indices, 
  * Bytes of global workspace glm53_sparse_mla_fwd_ws needs for this shape on
  * the current device (0 when each token runs on a single CTA). Resolves
  * splits == 0 exactly as the forward does. The size is
- * T * splits * (Hp * 512 + 2 * Hp) * 4 bytes, Hp = max(H, 16): 16 MiB for a
- * 32-token, 64-head decode batch split 4 ways.
+ * T * splits * Hp * 512 * 4 bytes, Hp = max(H, 16): 16 MiB for a 32-token,
+ * 64-head decode batch split 4 ways.
  * No counterpart in the reference, whose kernel never splits a token.
  */
 int glm53_sparse_mla_workspace_bytes(int64_t T, int64_t H, int64_t topk, int splits,
@@ -120,7 +120,7 @@ int glm53_sparse_mla_fwd_ws(const void* q, const void* kv, const int32_t* indice
  * (glm53_sparse_mla_workspace_bytes) exceeds 32 MiB is rejected with
  * GLM53_ERR_SCRATCH_LIMIT before any launch. With automatic splitting a
  * launch that splits its tokens has at most one CTA per SM (148 on B200),
- * which needs at most 18.6 MiB.
+ * which needs at most 18.5 MiB.
  * The first call on each device looks up the array's device address (and
  * sets the kernels' shared-memory limit); make that first call before any
  * stream capture. All calls share the one array and it keeps the previous

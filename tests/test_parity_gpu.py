@@ -295,7 +295,7 @@ def test_workspace_contract():
     w = W.config_c2(device="cuda")
     nb = ctypes.c_uint64(0)
     assert lib.glm53_sparse_mla_workspace_bytes(w.T, w.H, w.topk, 4, ctypes.byref(nb)) == 0
-    assert nb.value == w.T * 4 * (64 * 512 + 2 * 64) * 4
+    assert nb.value == w.T * 4 * 64 * 512 * 4
     assert lib.glm53_sparse_mla_workspace_bytes(w.T, w.H, w.topk, 1, ctypes.byref(nb)) == 0
     assert nb.value == 0
     rc, _, need = abi_fwd_ws(lib, w, 4, ws_bytes=0)

@@ -75,8 +75,8 @@ def test_noalloc_matches_fwd_on_two_calls_in_a_row():
 def test_noalloc_refuses_shapes_beyond_its_scratch():
     lib = _lib()
     w = next(iter(W.case_matrix(heads=64, topk=2048, rows=8192, device="cuda", seed=23)))
-    # 8 CTAs per token x 64 heads needs T * 8 * 131,584 B of scratch: above 32 MiB once
-    # T > 31, so a 64-token batch is refused before anything is launched.
+    # 8 CTAs per token x 64 heads needs T * 8 * 131,072 B of scratch: above 32 MiB once
+    # T > 32, so a 64-token batch is refused before anything is launched.
     q = w.q.repeat(64 // w.T + 1, 1, 1)[:64].contiguous()
     idx = w.indices.repeat(64 // w.T + 1, 1)[:64].contiguous()
     big = W.Workload("big", q, w.kv, idx, w.sm_scale)

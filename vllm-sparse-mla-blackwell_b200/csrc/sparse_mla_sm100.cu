@@ -9,11 +9,13 @@
 //   partial results are merged through distributed shared memory at the end,
 //   so no global scratch and no second launch are needed.
 //
-// Per CTA (256 threads, one CTA per SM, ~219 KB shared memory)
-//   warps 0-3  softmax, GEMM2 issue, epilogue (warp w owns TMEM lanes 32w..)
-//   warps 4-6  gather: bf16 KV by 16-byte cp.async, fp8 KV by register loads
-//              + dequantisation, into a 2-stage ring
-//   warp  7    TMEM allocator + GEMM1 issuer (one lane)
+// Per CTA (384 threads, one CTA per SM, ~222 KB shared memory)
+//   warps 0-3   softmax, GEMM2 issue, epilogue (warp w owns TMEM lanes 32w..)
+//   warps 4-10  gather: bf16 KV by 16-byte cp.async, fp8 KV by register loads
+//               + dequantisation, into a 2-stage ring (seven warps: a 64 KB
+//               tile is issued in about half the time three warps need)
+//   warp  11    TMEM allocator + GEMM1 issuer (one lane)
+//   all warps gather the first two tiles; warps 0-7 run the split merge
 //
 // Index handling: the CTA first compacts its chunk of the index list to the
 // valid entries (order preserved), so masked indices cost neither bandwidth
@@ -57,6 +59,7 @@
 #include <cstdint>
 #include <cstdlib>
 #include <mutex>
+#include <type_traits>
 
 #include "glm53_sparse_mla.h"
 #include "sm100_ptx.cuh"
@@ -66,11 +69,11 @@ namespace glm53 {
 constexpr int kDim = 512;           // latent width = head size
 constexpr int kRows = 64;           // KV rows per pipeline tile
 constexpr int kMaxChunk = 2048;     // indices one CTA can hold after compaction
-constexpr int kThreads = 256;       // 8 warps (a 288-thread CTA caps registers at 168)
-constexpr int kProducerWarp0 = 4;   // warps 4-6 gather
-constexpr int kProducerWarps = 3;
+constexpr int kThreads = 384;       // 12 warps
+constexpr int kProducerWarp0 = 4;   // warps 4-10 gather
+constexpr int kProducerWarps = 7;
 constexpr int kProducerThreads = 32 * kProducerWarps;
-constexpr int kMmaWarp = 7;
+constexpr int kMmaWarp = 11;
 constexpr int kTmemCols = 512;
 constexpr uint32_t kTmemS = 256;    // S double buffer at columns 256 and 320
 constexpr float kRescaleThreshold = 8.0f;   // log2 units: rescale when max grows > 256x
@@ -85,19 +88,21 @@ constexpr uint32_t kSmIdx = kSmP + 2 * kPBytes;       // int32[kMaxChunk]
 constexpr uint32_t kSmHead = kSmIdx + 4 * kMaxChunk;  // m[64] l[64] alpha[64] f[64]
 constexpr uint32_t kSmBar = kSmHead + 4 * 64 * 4;     // mbarriers
 constexpr uint32_t kSmMisc = kSmBar + 16 * 8;         // tmem base, counts, abort flag
-constexpr uint32_t kSmUsed = kSmMisc + 64;
+constexpr uint32_t kSmMlRecv = kSmMisc + 64;         // m[8][64], l[8][64] of the split peers
+constexpr uint32_t kSmUsed = kSmMlRecv + 2 * 8 * 64 * 4;
 constexpr uint32_t kSmemBytes = kSmUsed + 1024;       // + slack to align the base
 
 // mbarrier slots
 enum : int {
-  kBarKvFull = 0,    // [2] producers -> MMA: stage loaded
+  kBarKvFull = 0,    // [2] producers -> GEMM1 issuer: stage of tile >= 2 loaded
   kBarKvEmpty = 2,   // [2] GEMM2 (4 commits) -> producers: stage consumed
   kBarSFull = 4,     // [2] GEMM1 (commit) -> softmax: S ready
   kBarSEmpty = 6,    // [2] softmax -> GEMM1 issuer: S buffer read
   kBarODone = 10,    // GEMM2 (4 commits) -> softmax: a GEMM2 finished
   kBarDrain = 11,    // GEMM1 issuer's UMMAs all retired
   kBarQFull = 12,    // all threads (cp.async) -> GEMM1 issuer: Q landed
-  kNumBars = 13
+  kBarKvFirst = 13,  // [2] all threads -> GEMM1 issuer: tile 0 / 1 loaded
+  kNumBars = 15
 };
 
 // misc words
@@ -202,6 +207,8 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
     mbar_init(bar(kBarODone), 4);
     mbar_init(bar(kBarDrain), 1);
     mbar_init(bar(kBarQFull), kThreads);
+    mbar_init(bar(kBarKvFirst), kThreads);
+    mbar_init(bar(kBarKvFirst + 1), kThreads);
     misc[kMiscAbort] = 0;
     fence_mbarrier_init();
   }
@@ -293,68 +300,73 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
               sdesc_sw128(pbuf + kk * 32u, 16, 1024), kIdesc2, (t > 0 || kk > 0) ? 1u : 0u);
   };
 
-  // ------------------------------------------------------------------ roles
-  if (warp >= kProducerWarp0 && warp < kMmaWarp) {
-    // ================= gather =================
-    const int pw = warp - kProducerWarp0;
-    auto recycle = [&](int t) -> bool {   // stage of tile t is free again
-      return t < 2 ||
-             mbar_wait_bounded(bar(kBarKvEmpty + (t & 1)), ((t >> 1) - 1) & 1, abort_flag, p.timeout_ns);
-    };
+  // Gather rows r = r0, r0 + step, ... of tile t into its stage: bf16 rows by
+  // 16-byte cp.async per lane (half a row per warp instruction; the last
+  // tile's missing rows are zero-filled through src-size 0), fp8 rows by
+  // 16-byte register loads, e4m3 -> bf16 (x kv_scale) in registers and
+  // swizzled 16-byte shared stores. Then arrive on `full`: bf16 through the
+  // deferred cp.async arrive (fires once this thread's copies have landed),
+  // fp8 after a proxy fence.
+  auto gather_rows = [&](int t, int r0, auto step_c, uint32_t full) {
+    constexpr int kStep = decltype(step_c)::value;
+    const uint32_t stage = sb + kSmKV + (t & 1) * kStageBytes;
+    const int rows = min(kRows, n_valid - kRows * t);
     if constexpr (!kFp8) {
-      // 16-byte cp.async per lane, half a row per warp instruction; the
-      // deferred arrive (.noinc) completes the stage once this thread's copies
-      // land. The last tile's missing rows are zero-filled (src-size 0).
       const uint8_t* kvb = static_cast<const uint8_t*>(p.kv);
-      for (int t = 0; t < n_tiles; ++t) {
-        const int s = t & 1;
-        if (!recycle(t)) break;
-        const uint32_t stage = sb + kSmKV + s * kStageBytes;
-        const int rows = min(kRows, n_valid - kRows * t);
 #pragma unroll 4
-        for (int r = pw; r < kRows; r += kProducerWarps) {
-          const bool valid = r < rows;
-          const long long row = valid ? idx_sm[kRows * t + r] : 0;
-          const uint8_t* src = kvb + row * (kDim * 2);
+      for (int r = r0; r < kRows; r += kStep) {
+        const bool valid = r < rows;
+        const long long row = valid ? idx_sm[kRows * t + r] : 0;
+        const uint8_t* src = kvb + row * (kDim * 2);
 #pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            const int c = lane + 32 * hh;
-            cp_async_16(stage + swz(r, c), src + c * 16, valid ? 16u : 0u);
-          }
+        for (int hh = 0; hh < 2; ++hh) {
+          const int c = lane + 32 * hh;
+          cp_async_16(stage + swz(r, c), src + c * 16, valid ? 16u : 0u);
         }
-        cp_async_mbar_arrive_noinc(bar(kBarKvFull + s));
       }
+      cp_async_mbar_arrive_noinc(full);
     } else {
       const uint8_t* kv8 = static_cast<const uint8_t*>(p.kv);
-      for (int t = 0; t < n_tiles; ++t) {
-        const int s = t & 1;
-        if (!recycle(t)) break;
-        const uint32_t stage = sb + kSmKV + s * kStageBytes;
-        const int rows = min(kRows, n_valid - kRows * t);
-        constexpr int kPer = (kRows + kProducerWarps - 1) / kProducerWarps;
-        uint4 buf[kPer];
+      constexpr int kPer = (kRows + kStep - 1) / kStep;
+      uint4 buf[kPer];
 #pragma unroll
-        for (int j = 0; j < kPer; ++j) {
-          const int r = pw + kProducerWarps * j;
-          if (r < rows) {
-            const long long row = idx_sm[kRows * t + r];
-            buf[j] = ldg_nc_v4(kv8 + row * kDim + lane * 16);
-          } else {
-            buf[j] = make_uint4(0u, 0u, 0u, 0u);
-          }
+      for (int j = 0; j < kPer; ++j) {
+        const int r = r0 + kStep * j;
+        if (r < rows) {
+          const long long row = idx_sm[kRows * t + r];
+          buf[j] = ldg_nc_v4(kv8 + row * kDim + lane * 16);
+        } else {
+          buf[j] = make_uint4(0u, 0u, 0u, 0u);
         }
+      }
 #pragma unroll
-        for (int j = 0; j < kPer; ++j) {
-          const int r = pw + kProducerWarps * j;
-          if (r >= kRows) break;
+      for (int j = 0; j < kPer; ++j) {
+        const int r = r0 + kStep * j;
+        if (r < kRows) {
           uint4 lo, hi;
           dequant16(buf[j], p.kv_scale, lo, hi);
           sts_v4(stage + swz(r, 2 * lane), lo);
           sts_v4(stage + swz(r, 2 * lane + 1), hi);
         }
-        fence_proxy_async_smem();
-        mbar_arrive(bar(kBarKvFull + s));
       }
+      fence_proxy_async_smem();
+      mbar_arrive(full);
+    }
+  };
+
+  // Both stages are empty at the start: every warp gathers tiles 0 and 1
+  // (each warp a row in 8), which brings the first GEMM1 forward.
+  for (int t = 0; t < min(2, n_tiles); ++t)
+    gather_rows(t, warp, std::integral_constant<int, kThreads / 32>{}, bar(kBarKvFirst + t));
+
+  // ------------------------------------------------------------------ roles
+  if (warp >= kProducerWarp0 && warp < kMmaWarp) {
+    // ================= gather (tiles 2, 3, ...) =================
+    const int pw = warp - kProducerWarp0;
+    for (int t = 2; t < n_tiles; ++t) {
+      if (!mbar_wait_bounded(bar(kBarKvEmpty + (t & 1)), ((t >> 1) - 1) & 1, abort_flag, p.timeout_ns))
+        break;
+      gather_rows(t, pw, std::integral_constant<int, kProducerWarps>{}, bar(kBarKvFull + (t & 1)));
     }
     __syncwarp();
   } else if (warp == kMmaWarp) {
@@ -365,7 +377,9 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
     if (lane == 0) {
       bool ok = n_tiles == 0 || mbar_wait_bounded(bar(kBarQFull), 0, abort_flag, p.timeout_ns);
       for (int g1 = 0; ok && g1 < n_tiles; ++g1) {
-        ok = mbar_wait_bounded(bar(kBarKvFull + (g1 & 1)), (g1 >> 1) & 1, abort_flag, p.timeout_ns) &&
+        ok = (g1 < 2 ? mbar_wait_bounded(bar(kBarKvFirst + g1), 0, abort_flag, p.timeout_ns)
+                     : mbar_wait_bounded(bar(kBarKvFull + (g1 & 1)), ((g1 >> 1) - 1) & 1, abort_flag,
+                                         p.timeout_ns)) &&
              (g1 < 2 ||
               mbar_wait_bounded(bar(kBarSEmpty + (g1 & 1)), ((g1 >> 1) - 1) & 1, abort_flag, p.timeout_ns));
         if (!ok) break;
@@ -427,27 +441,18 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
         // O^T must hold GEMM2(t-1) in full before it is rescaled.
         mbar_wait_bounded(bar(kBarODone), (t - 1) & 1, abort_flag, p.timeout_ns);
         tc_fence_after();
-#pragma unroll
+        // 16 columns at a time: the S values of this tile stay live here
+#pragma unroll 1
         for (int m = 0; m < 4; ++m) {
-          if constexpr (NH == 16) {
+#pragma unroll
+          for (int cc = 0; cc < NH / 16; ++cc) {
             float o[16];
-            const uint32_t ta = tmem + lane_base + static_cast<uint32_t>(m * NH);
+            const uint32_t ta = tmem + lane_base + static_cast<uint32_t>(m * NH + 16 * cc);
             tmem_ld_32x32b_x16(ta, o);
             tmem_wait_ld();
 #pragma unroll
-            for (int j = 0; j < 16; ++j) o[j] *= alpha_sm[j];
+            for (int j = 0; j < 16; ++j) o[j] *= alpha_sm[16 * cc + j];
             tmem_st_32x32b_x16(ta, o);
-          } else {
-#pragma unroll
-            for (int cc = 0; cc < NH / 32; ++cc) {
-              float o[32];
-              const uint32_t ta = tmem + lane_base + static_cast<uint32_t>(m * NH + 32 * cc);
-              tmem_ld_32x32b_x32(ta, o);
-              tmem_wait_ld();
-#pragma unroll
-              for (int j = 0; j < 32; ++j) o[j] *= alpha_sm[32 * cc + j];
-              tmem_st_32x32b_x32(ta, o);
-            }
           }
         }
         tmem_wait_st();
@@ -537,21 +542,23 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
     // ---- split across 2, 4 or 8 CTAs, merged through a global workspace
     // (it stays in L2). Each CTA owns a d-slice of the output. All 8 warps
     // work: warp w reads TMEM lane quadrant w & 3 and head half w >> 2 (at
-    // NH = 16, warps 0-3 take all heads). Workspace per (token, CTA): m[NH],
-    // l[NH], then one slice per destination CTA laid out [NH / 4][dspan][4]
-    // floats, so a warp's 16-byte stores and loads cover 512 contiguous bytes.
-    // Every slice is written before the cluster barrier and read after it,
-    // so the workspace needs no initialisation.
+    // NH = 16, warps 0-3 take all heads). Per-head (max, sum) pairs go to
+    // every peer's shared memory (a few hundred bytes); the partials go to
+    // the workspace, per (token, CTA) one slice per destination CTA laid out
+    // [NH / 4][dspan][4] floats, so a warp's 16-byte stores and loads cover
+    // 512 contiguous bytes. Every slice is written before the cluster barrier
+    // and read after it, so the workspace needs no initialisation.
     constexpr int kHalf = NH >= 32 ? NH / 2 : NH;
+    constexpr int kV = kHalf / 4;                   // float4 per (d, peer)
     const int dspan = kDim / nranks;
-    const size_t blk = static_cast<size_t>(NH) * kDim + 2 * NH;   // floats per (token, CTA)
+    const size_t blk = static_cast<size_t>(NH) * kDim;   // floats per (token, CTA)
     float* const ws_tok = p.ws + static_cast<size_t>(token) * nranks * blk;
-    float* const ws_me = ws_tok + static_cast<size_t>(split) * blk;
     const int qd = warp & 3;
-    const bool active = NH >= 32 || warp < 4;
+    const bool active = warp < (NH >= 32 ? 8 : 4);
     const int h0 = NH >= 32 ? (warp >> 2) * kHalf : 0;
     const uint32_t tcol = static_cast<uint32_t>(32 * qd) << 16;
     float* const scal = reinterpret_cast<float*>(gb + kSmIdx);   // e[8][NH], 1/L[NH]
+    const float* const ml = reinterpret_cast<const float*>(gb + kSmMlRecv);   // m[8][64], l[8][64]
     auto load_half = [=](int m, float (&o)[kHalf]) {
       const uint32_t ta = tmem + tcol + static_cast<uint32_t>(m * NH + h0);
       if constexpr (kHalf == 32) {
@@ -566,8 +573,12 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
     __syncthreads();   // every role past its main loop; m_sm / l_sm written
     tc_fence_after();
     if (tid < NH) {
-      stg_cg_f32(ws_me + tid, m_sm[tid]);
-      stg_cg_f32(ws_me + NH + tid, l_sm[tid]);
+      const float mv = m_sm[tid], lv = l_sm[tid];
+      for (int q = 0; q < nranks; ++q) {
+        const uint32_t a = sb + kSmMlRecv + 4u * static_cast<uint32_t>(split * 64 + tid);
+        st_dsmem_f32(mapa_shared(a, q), mv);
+        st_dsmem_f32(mapa_shared(a + 4u * 8u * 64u, q), lv);
+      }
     }
     if (active) {
 #pragma unroll 1
@@ -581,40 +592,26 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
 #pragma unroll
           for (int j = 0; j < kHalf; ++j) o[j] = 0.f;
         }
-        float* const dst = ws_me + 2 * NH + static_cast<size_t>(owner) * NH * dspan;
+        float* const dst = ws_tok + static_cast<size_t>(split) * blk + static_cast<size_t>(owner) * NH * dspan;
         const int dl = d - owner * dspan;
 #pragma unroll
-        for (int c = 0; c < kHalf / 4; ++c)
+        for (int c = 0; c < kV; ++c)
           stg_cg_f4(dst + (static_cast<size_t>(h0 / 4 + c) * dspan + dl) * 4,
                     make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]));
       }
     }
     __threadfence();
-    cluster_sync_all();   // every CTA's workspace stores visible cluster-wide
+    cluster_sync_all();   // every CTA's (max, sum) and workspace stores visible
     if (tid < NH) {
-      float mr[8], lr[8];
       float M = -INFINITY;
-#pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        if (r < nranks) {
-          if (r == split) {
-            mr[r] = m_sm[tid];
-            lr[r] = l_sm[tid];
-          } else {
-            mr[r] = ldg_cg_f32(ws_tok + r * blk + tid);
-            lr[r] = ldg_cg_f32(ws_tok + r * blk + NH + tid);
-          }
-          if (lr[r] > 0.f) M = fmaxf(M, mr[r]);
-        }
-      }
+      for (int r = 0; r < nranks; ++r)
+        if (ml[512 + r * 64 + tid] > 0.f) M = fmaxf(M, ml[r * 64 + tid]);
       float L = 0.f;
-#pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        if (r < nranks) {
-          const float e = lr[r] > 0.f ? exp2f(mr[r] - M) : 0.f;
-          scal[r * NH + tid] = e;
-          L += lr[r] * e;
-        }
+      for (int r = 0; r < nranks; ++r) {
+        const float lr = ml[512 + r * 64 + tid];
+        const float e = lr > 0.f ? exp2f(ml[r * 64 + tid] - M) : 0.f;
+        scal[r * NH + tid] = e;
+        L += lr * e;
       }
       scal[8 * NH + tid] = L > 0.f ? 1.f / L : 0.f;
       if (split == 0 && p.lse != nullptr && tid < p.H)
@@ -627,29 +624,49 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
         const int d = 128 * m + 32 * qd + lane;
         if (d / dspan != split) continue;          // warp-uniform
         const int dl = d - split * dspan;
-        float o[kHalf];
-        load_half(m, o);
+        // 16 heads per pass keeps a pass's peer loads in registers
+#pragma unroll 1
+        for (int hp = 0; hp < kHalf; hp += 16) {
+          const int hb = h0 + hp;
+          const float* const src0 = ws_tok + static_cast<size_t>(split) * NH * dspan +
+                                    static_cast<size_t>(hb / 4) * dspan * 4 + dl * 4;
+          float o[16];
+          tmem_ld_32x32b_x16(tmem + tcol + static_cast<uint32_t>(m * NH + hb), o);
+          tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < kHalf; ++j) o[j] = n_tiles > 0 ? o[j] * scal[split * NH + h0 + j] : 0.f;
-        for (int r = 0; r < nranks; ++r) {
-          if (r == split) continue;
-          const float* src = ws_tok + r * blk + 2 * NH + static_cast<size_t>(split) * NH * dspan;
-          float4 v[kHalf / 4];
+          for (int j = 0; j < 16; ++j) o[j] = n_tiles > 0 ? o[j] * scal[split * NH + hb + j] : 0.f;
+          // peers in batches of three, each batch's loads issued together
+#pragma unroll 1
+          for (int i0 = 0; i0 < nranks - 1; i0 += 3) {
+            float4 v[3][4];
 #pragma unroll
-          for (int c = 0; c < kHalf / 4; ++c)
-            v[c] = ldg_cg_f4(src + (static_cast<size_t>(h0 / 4 + c) * dspan + dl) * 4);
+            for (int i = 0; i < 3; ++i) {
+              const int r = i0 + i < split ? i0 + i : i0 + i + 1;
+              if (i0 + i < nranks - 1) {
 #pragma unroll
-          for (int c = 0; c < kHalf / 4; ++c) {
-            const float* e = scal + r * NH + h0 + 4 * c;
-            o[4 * c] += v[c].x * e[0];
-            o[4 * c + 1] += v[c].y * e[1];
-            o[4 * c + 2] += v[c].z * e[2];
-            o[4 * c + 3] += v[c].w * e[3];
+                for (int c = 0; c < 4; ++c)
+                  v[i][c] = ldg_cg_f4(src0 + static_cast<size_t>(r) * blk + static_cast<size_t>(c) * dspan * 4);
+              }
+            }
+#pragma unroll
+            for (int i = 0; i < 3; ++i) {
+              const int r = i0 + i < split ? i0 + i : i0 + i + 1;
+              if (i0 + i < nranks - 1) {
+                const float* e = scal + r * NH + hb;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                  o[4 * c] += v[i][c].x * e[4 * c];
+                  o[4 * c + 1] += v[i][c].y * e[4 * c + 1];
+                  o[4 * c + 2] += v[i][c].z * e[4 * c + 2];
+                  o[4 * c + 3] += v[i][c].w * e[4 * c + 3];
+                }
+              }
+            }
           }
-        }
 #pragma unroll
-        for (int j = 0; j < kHalf; ++j) o[j] *= scal[8 * NH + h0 + j];
-        store_pairs_n<kHalf>(o_tok, p.H, d, h0, o);
+          for (int j = 0; j < 16; ++j) o[j] *= scal[8 * NH + hb + j];
+          store_pairs_n<16>(o_tok, p.H, d, hb, o);
+        }
       }
     }
     tc_fence_before();
@@ -770,31 +787,36 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
         const int m = split * (4 / nranks) + mm;
         const int d = 128 * m + 32 * warp + lane;
         const int dl = d - split * dspan;
-        float o[NH];
-        if (n_tiles > 0) {
-          load_o(m, o);
-        } else {
+#pragma unroll 1
+        for (int hb = 0; hb < NH; hb += 16) {   // 16 heads at a time
+          float o[16];
+          if (n_tiles > 0) {
+            tmem_ld_32x32b_x16(tmem + lane_base + static_cast<uint32_t>(m * NH + hb), o);
+            tmem_wait_ld();
+          } else {
 #pragma unroll
-          for (int j = 0; j < NH; ++j) o[j] = 0.f;
-        }
-#pragma unroll
-        for (int j = 0; j < NH; ++j) o[j] *= scal[split * NH + j];
-        for (int r = 0; r < nranks; ++r) {
-          if (r == split) continue;
-          const float4* row = reinterpret_cast<const float4*>(
-              gb + (r < split ? r : r - 1) * slot_bytes + 4u * (2 * NH + dl * NH));
-#pragma unroll
-          for (int c = 0; c < NH / 4; ++c) {
-            const float4 v = row[row_chunk(dl, c)];
-            o[4 * c] += v.x * scal[r * NH + 4 * c];
-            o[4 * c + 1] += v.y * scal[r * NH + 4 * c + 1];
-            o[4 * c + 2] += v.z * scal[r * NH + 4 * c + 2];
-            o[4 * c + 3] += v.w * scal[r * NH + 4 * c + 3];
+            for (int j = 0; j < 16; ++j) o[j] = 0.f;
           }
-        }
 #pragma unroll
-        for (int j = 0; j < NH; ++j) o[j] *= scal[4 * NH + j];
-        store_pairs(d, o);
+          for (int j = 0; j < 16; ++j) o[j] *= scal[split * NH + hb + j];
+          for (int r = 0; r < nranks; ++r) {
+            if (r == split) continue;
+            const float4* row = reinterpret_cast<const float4*>(
+                gb + (r < split ? r : r - 1) * slot_bytes + 4u * (2 * NH + dl * NH));
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const float4 v = row[row_chunk(dl, hb / 4 + c)];
+              const float* e = scal + r * NH + hb + 4 * c;
+              o[4 * c] += v.x * e[0];
+              o[4 * c + 1] += v.y * e[1];
+              o[4 * c + 2] += v.z * e[2];
+              o[4 * c + 3] += v.w * e[3];
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < 16; ++j) o[j] *= scal[4 * NH + hb + j];
+          store_pairs_n<16>(o_tok, p.H, d, hb, o);
+        }
       }
       tc_fence_before();
     }
@@ -1030,7 +1052,7 @@ int resolve_splits(int64_t T, int64_t topk, int splits, int dev) {
 uint64_t workspace_floats(int64_t T, int64_t H, int splits) {
   if (splits <= 1) return 0;
   const uint64_t nh = static_cast<uint64_t>(padded_heads(H));
-  return static_cast<uint64_t>(T) * static_cast<uint64_t>(splits) * (nh * kDim + 2 * nh);
+  return static_cast<uint64_t>(T) * static_cast<uint64_t>(splits) * nh * kDim;
 }
 
 // Shared body of the forward entry points. `ws == nullptr` selects the
