@@ -136,6 +136,12 @@ __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
   return v;
 }
 
+__device__ __forceinline__ uint2 ldg_nc_v2(const void* p) {
+  uint2 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+  return v;
+}
+
 __device__ __forceinline__ void sts_v4(uint32_t addr, uint4 v) {
   asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(v.x), "r"(v.y),
                "r"(v.z), "r"(v.w)
@@ -173,6 +179,17 @@ __device__ __forceinline__ float ldg_cg_f32(const float* p) {
   float v;
   asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
   return v;
+}
+
+// Programmatic dependent launch: wait until the grids this one depends on
+// have completed and their memory is visible (a no-op without such a
+// dependency), and allow the next grid in the stream to start launching.
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // Order this thread's generic-proxy shared-memory accesses before later

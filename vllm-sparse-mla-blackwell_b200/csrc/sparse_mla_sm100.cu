@@ -145,15 +145,10 @@ __device__ __forceinline__ uint32_t dequant2(uint32_t two, float scale) {
   return pack_bf16x2(f.x * scale, f.y * scale);
 }
 
-__device__ __forceinline__ void dequant16(const uint4 w, float scale, uint4& lo, uint4& hi) {
-  lo.x = dequant2(w.x & 0xFFFFu, scale);
-  lo.y = dequant2(w.x >> 16, scale);
-  lo.z = dequant2(w.y & 0xFFFFu, scale);
-  lo.w = dequant2(w.y >> 16, scale);
-  hi.x = dequant2(w.z & 0xFFFFu, scale);
-  hi.y = dequant2(w.z >> 16, scale);
-  hi.z = dequant2(w.w & 0xFFFFu, scale);
-  hi.w = dequant2(w.w >> 16, scale);
+// Eight e4m3 values (one 16-byte bf16 chunk) -> bf16 x scale.
+__device__ __forceinline__ uint4 dequant8(const uint2 w, float scale) {
+  return make_uint4(dequant2(w.x & 0xFFFFu, scale), dequant2(w.x >> 16, scale),
+                    dequant2(w.y & 0xFFFFu, scale), dequant2(w.y >> 16, scale));
 }
 
 // bf16 store of out[h0 + j][d] for j < N: neighbouring lanes (d, d ^ 1) swap
@@ -217,6 +212,9 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
     tmem_relinquish();
   }
   __syncthreads();   // barriers initialised before anyone arrives on them
+  // With programmatic dependent launch the set-up above overlaps the previous
+  // grid's tail; nothing global is read or written before this point.
+  griddep_wait();
 
   // Index compaction, pass 1: warps 0-7 each take a contiguous sub-range of
   // this CTA's chunk, keep it in registers and count the valid entries.
@@ -326,27 +324,29 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
       }
       cp_async_mbar_arrive_noinc(full);
     } else {
+      // lane l owns bf16 chunks l and l + 32 of each row (fp8 bytes 8l and
+      // 256 + 8l): a warp's loads cover 256 contiguous bytes and a
+      // quarter-warp's swizzled 16-byte stores hit 8 distinct bank groups
       const uint8_t* kv8 = static_cast<const uint8_t*>(p.kv);
       constexpr int kPer = (kRows + kStep - 1) / kStep;
-      uint4 buf[kPer];
+      uint2 buf[kPer][2];
 #pragma unroll
       for (int j = 0; j < kPer; ++j) {
         const int r = r0 + kStep * j;
         if (r < rows) {
-          const long long row = idx_sm[kRows * t + r];
-          buf[j] = ldg_nc_v4(kv8 + row * kDim + lane * 16);
+          const uint8_t* src = kv8 + static_cast<long long>(idx_sm[kRows * t + r]) * kDim + lane * 8;
+          buf[j][0] = ldg_nc_v2(src);
+          buf[j][1] = ldg_nc_v2(src + 256);
         } else {
-          buf[j] = make_uint4(0u, 0u, 0u, 0u);
+          buf[j][0] = buf[j][1] = make_uint2(0u, 0u);
         }
       }
 #pragma unroll
       for (int j = 0; j < kPer; ++j) {
         const int r = r0 + kStep * j;
         if (r < kRows) {
-          uint4 lo, hi;
-          dequant16(buf[j], p.kv_scale, lo, hi);
-          sts_v4(stage + swz(r, 2 * lane), lo);
-          sts_v4(stage + swz(r, 2 * lane + 1), hi);
+          sts_v4(stage + swz(r, lane), dequant8(buf[j][0], p.kv_scale));
+          sts_v4(stage + swz(r, lane + 32), dequant8(buf[j][1], p.kv_scale));
         }
       }
       fence_proxy_async_smem();
@@ -504,6 +504,9 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
   }
 
   // ------------------------------------------------------------------ merge
+  // Every CTA of this grid is resident by now, so the next grid in the stream
+  // may start launching (its CTAs wait in griddep_wait for this one to end).
+  griddep_launch_dependents();
   const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
   __nv_bfloat16* const o_tok = p.out + static_cast<size_t>(token) * p.H * kDim;
   const bool odd = lane & 1;
@@ -952,13 +955,15 @@ cudaError_t launch_fwd(const Params& p, int splits, cudaStream_t stream) {
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = kSmemBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = static_cast<unsigned>(splits);
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = splits > 1 ? 1 : 0;
+  cfg.numAttrs = splits > 1 ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, sparse_mla_fwd_kernel<NH, FP8>, p);
 }
 
