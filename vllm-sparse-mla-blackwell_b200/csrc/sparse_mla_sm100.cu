@@ -362,11 +362,77 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
   // ------------------------------------------------------------------ roles
   if (warp >= kProducerWarp0 && warp < kMmaWarp) {
     // ================= gather (tiles 2, 3, ...) =================
+    // bf16: cp.async into the stage once it is free (gather_rows); its writes
+    // land spread out as the data arrives.
+    // fp8: register-staged with one tile of prefetch: the rows of tile t + 1
+    // are loaded right after tile t is stored, so their DRAM latency runs
+    // while the stage they go to is still being consumed, and dequantised
+    // (x kv_scale) at store time. (Staging bf16 the same way measured slower:
+    // its 64 KB burst of shared stores stalls the tensor core's operand reads.)
+    // Lane l owns the 16-byte bf16 chunks l and l + 32 of each of its rows: a
+    // warp's loads cover 256 contiguous bytes and a quarter-warp's swizzled
+    // stores hit 8 distinct bank groups.
     const int pw = warp - kProducerWarp0;
-    for (int t = 2; t < n_tiles; ++t) {
-      if (!mbar_wait_bounded(bar(kBarKvEmpty + (t & 1)), ((t >> 1) - 1) & 1, abort_flag, p.timeout_ns))
-        break;
-      gather_rows(t, pw, std::integral_constant<int, kProducerWarps>{}, bar(kBarKvFull + (t & 1)));
+    constexpr int kPer = (kRows + kProducerWarps - 1) / kProducerWarps;
+    using Chunk = typename std::conditional<kFp8, uint2, uint4>::type;
+    Chunk buf[kPer][2];   // only the fp8 path uses it
+    auto load_tile = [&](int t) {
+      const int rows = min(kRows, n_valid - kRows * t);
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        const int r = pw + kProducerWarps * j;
+        if (r < rows) {
+          const long long row = idx_sm[kRows * t + r];
+          if constexpr (kFp8) {
+            const uint8_t* src = static_cast<const uint8_t*>(p.kv) + row * kDim + lane * 8;
+            buf[j][0] = ldg_nc_v2(src);
+            buf[j][1] = ldg_nc_v2(src + 256);
+          } else {
+            const uint8_t* src = static_cast<const uint8_t*>(p.kv) + row * (2 * kDim) + lane * 16;
+            buf[j][0] = ldg_nc_v4(src);
+            buf[j][1] = ldg_nc_v4(src + 512);
+          }
+        } else {
+          if constexpr (kFp8) {
+            buf[j][0] = buf[j][1] = make_uint2(0u, 0u);
+          } else {
+            buf[j][0] = buf[j][1] = make_uint4(0u, 0u, 0u, 0u);
+          }
+        }
+      }
+    };
+    auto store_tile = [&](int t) {
+      const uint32_t stage = sb + kSmKV + (t & 1) * kStageBytes;
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        const int r = pw + kProducerWarps * j;
+        if (r < kRows) {
+          if constexpr (kFp8) {
+            sts_v4(stage + swz(r, lane), dequant8(buf[j][0], p.kv_scale));
+            sts_v4(stage + swz(r, lane + 32), dequant8(buf[j][1], p.kv_scale));
+          } else {
+            sts_v4(stage + swz(r, lane), buf[j][0]);
+            sts_v4(stage + swz(r, lane + 32), buf[j][1]);
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(bar(kBarKvFull + (t & 1)));
+    };
+    if constexpr (kFp8) {
+      if (n_tiles > 2) load_tile(2);
+      for (int t = 2; t < n_tiles; ++t) {
+        if (!mbar_wait_bounded(bar(kBarKvEmpty + (t & 1)), ((t >> 1) - 1) & 1, abort_flag, p.timeout_ns))
+          break;
+        store_tile(t);
+        if (t + 1 < n_tiles) load_tile(t + 1);
+      }
+    } else {
+      for (int t = 2; t < n_tiles; ++t) {
+        if (!mbar_wait_bounded(bar(kBarKvEmpty + (t & 1)), ((t >> 1) - 1) & 1, abort_flag, p.timeout_ns))
+          break;
+        gather_rows(t, pw, std::integral_constant<int, kProducerWarps>{}, bar(kBarKvFull + (t & 1)));
+      }
     }
     __syncwarp();
   } else if (warp == kMmaWarp) {
