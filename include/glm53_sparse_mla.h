@@ -62,9 +62,11 @@ enum glm53_device_status_bits {
  *
  * sm_scale is the natural-log softmax scale (the kernel multiplies by log2 e).
  * kv_scale multiplies dequantised fp8 values; it is ignored for bf16.
- * splits: 0 = automatic (or the GLM53_SPLITS environment variable, read once);
- * 1, 2, 4 or 8 = split each token's top-k list across that many CTAs of one
- * thread-block cluster.
+ * splits: 0 = automatic (or the GLM53_SPLITS environment variable, read once):
+ * small batches split every token; a batch with more tokens than SMs runs its
+ * whole waves unsplit and splits the tokens of the last, partial wave (two
+ * launches). 1, 2, 4 or 8 = split each token's top-k list across that many
+ * CTAs of one thread-block cluster.
  * H must be 8, 16, 32 or 64; head_dim and the kv width must be 512; topk must
  * be a multiple of 32 and at most 16384. T == 0 is a no-op.
  *
@@ -84,8 +86,9 @@ int glm53_sparse_mla_fwd(const void* q, const void* kv, const int32_t* indices, 
  * Bytes of global workspace glm53_sparse_mla_fwd_ws needs for this shape on
  * the current device (0 when each token runs on a single CTA). Resolves
  * splits == 0 exactly as the forward does. The size is
- * T * splits * Hp * 512 * 4 bytes, Hp = max(H, 16): 16 MiB for a 32-token,
- * 64-head decode batch split 4 ways.
+ * (split tokens) * splits * Hp * 512 * 4 bytes, Hp = max(H, 16): 16 MiB for a
+ * 32-token, 64-head decode batch split 4 ways. With splits == 0 and more
+ * tokens than SMs, only the tokens of the last, partial wave are split.
  * No counterpart in the reference, whose kernel never splits a token.
  */
 int glm53_sparse_mla_workspace_bytes(int64_t T, int64_t H, int64_t topk, int splits,

@@ -1120,10 +1120,40 @@ int resolve_splits(int64_t T, int64_t topk, int splits, int dev) {
   return g_env_splits > 0 ? g_env_splits : glm53_sparse_mla_auto_splits(T, topk, g_sm_count[dev]);
 }
 
+// Launch plan: tokens [0, t_main) with s_main CTAs each, then tokens
+// [t_main, T) with s_tail CTAs each. Automatic splitting of a batch too large
+// to split (more tokens than SMs) keeps whole waves unsplit and splits the
+// tokens of the last, partial wave so they fill the machine instead of
+// running on a few SMs at the end.
+struct Plan {
+  int64_t t_main;
+  int s_main;
+  int64_t t_tail;
+  int s_tail;
+};
+
+Plan make_plan(int64_t T, int64_t topk, int splits, int dev) {
+  Plan pl{T, resolve_splits(T, topk, splits, dev), 0, 1};
+  if (splits == 0 && g_env_splits <= 0 && pl.s_main == 1) {
+    const int64_t sms = g_sm_count[dev];
+    const int64_t full = (T / sms) * sms, rem = T - full;
+    if (full > 0 && rem > 0) {
+      int ts = 1;
+      while (ts < 8 && rem * (2 * ts) <= sms && topk / (2 * ts) >= 4 * kRows) ts *= 2;
+      if (ts > 1) pl = Plan{full, 1, rem, ts};
+    }
+  }
+  return pl;
+}
+
 uint64_t workspace_floats(int64_t T, int64_t H, int splits) {
   if (splits <= 1) return 0;
   const uint64_t nh = static_cast<uint64_t>(padded_heads(H));
   return static_cast<uint64_t>(T) * static_cast<uint64_t>(splits) * nh * kDim;
+}
+
+uint64_t workspace_floats(const Plan& pl, int64_t H) {
+  return workspace_floats(pl.t_main, H, pl.s_main) + workspace_floats(pl.t_tail, H, pl.s_tail);
 }
 
 // Shared body of the forward entry points. `ws == nullptr` selects the
@@ -1143,42 +1173,48 @@ int launch_forward(const void* q, const void* kv, const int32_t* indices, void* 
   int dev = 0;
   rc = prepare_current_device(&dev);
   if (rc != GLM53_OK) return rc;
-  const int s = resolve_splits(T, topk, splits, dev);
-  if ((topk + s - 1) / s > kMaxChunk) return GLM53_ERR_TOPK;
-  float* wsf = nullptr;
-  if (use_ws && s > 1) {
-    const uint64_t need = 4 * workspace_floats(T, H, s);
-    if (ws == nullptr || !aligned16(ws) || ws_bytes < need) return GLM53_ERR_WORKSPACE;
-    wsf = static_cast<float*>(ws);
-  }
-
-  Params p;
-  p.q = static_cast<const __nv_bfloat16*>(q);
-  p.kv = kv;
-  p.idx = indices;
-  p.out = static_cast<__nv_bfloat16*>(out);
-  p.lse = lse;
-  p.ws = wsf;
-  p.kv_rows = kv_rows;
-  p.T = static_cast<int>(T);
-  p.H = static_cast<int>(H);
-  p.topk = static_cast<int>(topk);
-  p.splits = s;
-  p.chunk = static_cast<int>((topk + s - 1) / s);
-  p.c = sm_scale * 1.4426950408889634f;
-  p.kv_scale = kv_dtype == GLM53_KV_BF16 ? 1.0f : kv_scale;
-  p.timeout_ns = g_timeout_ns;
+  const Plan pl = make_plan(T, topk, splits, dev);
+  if ((topk + pl.s_main - 1) / pl.s_main > kMaxChunk) return GLM53_ERR_TOPK;
+  const uint64_t need = 4 * workspace_floats(pl, H);
+  if (use_ws && need > 0 && (ws == nullptr || !aligned16(ws) || ws_bytes < need))
+    return GLM53_ERR_WORKSPACE;
 
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool fp8 = kv_dtype == GLM53_KV_FP8_E4M3;
-  cudaError_t e;
-  if (H <= 16)
-    e = fp8 ? launch_fwd<16, true>(p, s, st) : launch_fwd<16, false>(p, s, st);
-  else if (H == 32)
-    e = fp8 ? launch_fwd<32, true>(p, s, st) : launch_fwd<32, false>(p, s, st);
-  else
-    e = fp8 ? launch_fwd<64, true>(p, s, st) : launch_fwd<64, false>(p, s, st);
-  return e == cudaSuccess ? GLM53_OK : GLM53_ERR_CUDA;
+  const size_t q_tok = static_cast<size_t>(H) * kDim;   // bf16 elements per token of q / out
+  float* ws_next = use_ws ? static_cast<float*>(ws) : nullptr;
+  for (int part = 0; part < 2; ++part) {
+    const int64_t t0 = part == 0 ? 0 : pl.t_main;
+    const int64_t n = part == 0 ? pl.t_main : pl.t_tail;
+    const int s = part == 0 ? pl.s_main : pl.s_tail;
+    if (n == 0) continue;
+    Params p;
+    p.q = static_cast<const __nv_bfloat16*>(q) + t0 * q_tok;
+    p.kv = kv;
+    p.idx = indices + t0 * topk;
+    p.out = static_cast<__nv_bfloat16*>(out) + t0 * q_tok;
+    p.lse = lse != nullptr ? lse + t0 * H : nullptr;
+    p.ws = (use_ws && s > 1) ? ws_next : nullptr;
+    if (p.ws != nullptr) ws_next += workspace_floats(n, H, s);
+    p.kv_rows = kv_rows;
+    p.T = static_cast<int>(n);
+    p.H = static_cast<int>(H);
+    p.topk = static_cast<int>(topk);
+    p.splits = s;
+    p.chunk = static_cast<int>((topk + s - 1) / s);
+    p.c = sm_scale * 1.4426950408889634f;
+    p.kv_scale = kv_dtype == GLM53_KV_BF16 ? 1.0f : kv_scale;
+    p.timeout_ns = g_timeout_ns;
+    cudaError_t e;
+    if (H <= 16)
+      e = fp8 ? launch_fwd<16, true>(p, s, st) : launch_fwd<16, false>(p, s, st);
+    else if (H == 32)
+      e = fp8 ? launch_fwd<32, true>(p, s, st) : launch_fwd<32, false>(p, s, st);
+    else
+      e = fp8 ? launch_fwd<64, true>(p, s, st) : launch_fwd<64, false>(p, s, st);
+    if (e != cudaSuccess) return GLM53_ERR_CUDA;
+  }
+  return GLM53_OK;
 }
 
 }  // namespace glm53
@@ -1201,7 +1237,7 @@ extern "C" int glm53_sparse_mla_workspace_bytes(int64_t T, int64_t H, int64_t to
   int dev = 0;
   const int rc = prepare_current_device(&dev);
   if (rc != GLM53_OK) return rc;
-  *bytes = 4 * workspace_floats(T, H, resolve_splits(T, topk, splits, dev));
+  *bytes = 4 * workspace_floats(make_plan(T, topk, splits, dev), H);
   return GLM53_OK;
 }
 
@@ -1255,8 +1291,8 @@ extern "C" int glm53_sparse_mla_fwd_noalloc(const void* q, const void* kv, const
     }
     scratch = g_noalloc_addr[dev];
   }
-  const int s = resolve_splits(T, topk, splits, dev);
-  if (4 * workspace_floats(T, H, s) > kNoAllocScratchBytes) return GLM53_ERR_SCRATCH_LIMIT;
+  if (4 * workspace_floats(make_plan(T, topk, splits, dev), H) > kNoAllocScratchBytes)
+    return GLM53_ERR_SCRATCH_LIMIT;
   return launch_forward(q, kv, indices, out, lse, T, H, head_dim, kv_rows, kv_width, topk,
                         kv_dtype, sm_scale, kv_scale, splits, true, scratch, kNoAllocScratchBytes,
                         stream);
