@@ -154,6 +154,12 @@ __device__ __forceinline__ void stg_v4(void* p, uint4 v) {
                : "memory");
 }
 
+// Bulk prefetch of `bytes` (a multiple of 16, 16-byte aligned) from global
+// memory into L2; fire and forget, no registers or shared memory involved.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // 16-byte global store / load cached in L2 only (.cg): for data that other
 // CTAs of the same launch exchange through a workspace, never through L1.
 __device__ __forceinline__ void stg_cg_f4(void* p, float4 v) {

@@ -428,10 +428,21 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
         if (t + 1 < n_tiles) load_tile(t + 1);
       }
     } else {
+      // The rows of tile t + 1 are prefetched into L2 (one 1 KB bulk prefetch
+      // per row) as soon as tile t is issued, so when their stage frees the
+      // cp.async is served from L2 instead of waiting out DRAM latency.
+      const uint8_t* kvb = static_cast<const uint8_t*>(p.kv);
+      const int pt = tid - 32 * kProducerWarp0;   // 0 .. kProducerThreads - 1
+      auto prefetch_tile = [&](int t) {
+        const int rows = min(kRows, n_valid - kRows * t);
+        if (pt < rows) prefetch_l2_bulk(kvb + static_cast<long long>(idx_sm[kRows * t + pt]) * (2 * kDim), 2 * kDim);
+      };
+      if (n_tiles > 2) prefetch_tile(2);
       for (int t = 2; t < n_tiles; ++t) {
         if (!mbar_wait_bounded(bar(kBarKvEmpty + (t & 1)), ((t >> 1) - 1) & 1, abort_flag, p.timeout_ns))
           break;
         gather_rows(t, pw, std::integral_constant<int, kProducerWarps>{}, bar(kBarKvFull + (t & 1)));
+        if (t + 1 < n_tiles) prefetch_tile(t + 1);
       }
     }
     __syncwarp();
