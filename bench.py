@@ -279,9 +279,10 @@ def run_ours(args, dist: Dist):
             step(k)
     torch.cuda.synchronize()
 
-    # capture the K timed steps in one graph (launch-bound otherwise)
+    # capture the K timed steps in one graph (launch-bound otherwise); the
+    # NCCL all-gather of the head-sharded mode is captured with them
     graph = torch.cuda.CUDAGraph()
-    use_graph = gathered is None
+    use_graph = True
     if use_graph:
         with torch.cuda.graph(graph, stream=stream):
             for k in range(args.steps):
@@ -440,6 +441,12 @@ def run_reference(args, dist: Dist):
     oracle port) on the host cores, rank 0 only; other ranks exit at once."""
     if dist.rank != 0:
         return
+    # torchrun pins OMP threads to 1 per rank; the CPU arm uses every core
+    try:
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(limits=os.cpu_count() or 1)
+    except Exception:  # pragma: no cover
+        pass
     from glm53_sparse_mla import workloads as W
     device = "cuda" if torch.cuda.is_available() else "cpu"
     w = make_workload(args, W, 100, device, 0)
