@@ -8,7 +8,10 @@ oracle/sparse_mla_oracle.py on the same seeded inputs:
   * a fully masked token returns exact zeros and LSE -inf
   * fp8 KV is compared against the oracle run on the dequantised cache, so the
     test isolates the kernel's handling from fp8's own quantisation error
-    (the reference's tests/run_fp8.py:31-38 does the same).
+    (the reference's tests/run_fp8.py:31-38 does the same). The dequantisation
+    is exact (fp32), the values the kernel computes with; the reference's own
+    fp8 gate, against a bf16-rounded dequantisation with its 6e-3 / 0.9999
+    bounds, is checked as well (test_fp8_reference_gate).
 """
 
 from __future__ import annotations
@@ -28,19 +31,21 @@ import glm53_sparse_mla as G  # noqa: E402
 from glm53_sparse_mla import workloads as W  # noqa: E402
 
 
-def _kv_values(w: W.Workload) -> torch.Tensor:
+def _kv_values(w: W.Workload, exact: bool = True) -> torch.Tensor:
     if w.kv.dtype == torch.float8_e4m3fn:
-        return W.dequantize_fp8(w.kv, w.kv_scale)
+        return W.dequantize_fp8(w.kv, w.kv_scale, exact=exact)
     return w.kv
 
 
-def _oracle(w: W.Workload, rows_subset=None):
+def _oracle(w: W.Workload, rows_subset=None, exact: bool = True):
     """Oracle output / log2-LSE for all tokens (or a subset), reading back only
-    the KV rows the selected tokens reference."""
+    the KV rows the selected tokens reference. An fp8 cache is dequantised in
+    fp32 (the fp32 reference on the kernel's actual inputs), or with
+    ``exact=False`` rounded to bf16 as the reference's fp8 gate does."""
     idx = w.indices if rows_subset is None else w.indices[rows_subset]
     q = w.q if rows_subset is None else w.q[rows_subset]
     uniq, inv = torch.unique(idx.clamp_min(0).long(), return_inverse=True)
-    kv_rows = _kv_values(w)[uniq.to(w.kv.device)].float().cpu().numpy()
+    kv_rows = _kv_values(w, exact)[uniq.to(w.kv.device)].float().cpu().numpy()
     local = torch.where(idx >= 0, inv.to(idx.device).int(), torch.full_like(idx, -1))
     out, m, s = O.sparse_mla_stats(q.float().cpu().numpy(), kv_rows, local.cpu().numpy(),
                                    w.sm_scale)
@@ -307,3 +312,18 @@ def test_workspace_contract():
     torch.cuda.synchronize()
     ref, _ = _oracle(w)
     _check("c2/ws/s1", out, ref, w.indices)
+
+
+# the reference's fp8 gate (tests/run_fp8.py:23 of the reference): its bounds,
+# against the bf16-rounded dequantisation its kernel computes with
+REF_FP8_REL, REF_FP8_COS = 6e-3, 0.9999
+
+
+@pytest.mark.parametrize("heads", [64, 32, 16, 8])
+def test_fp8_reference_gate(heads):
+    for w in W.case_matrix(heads=heads, topk=2048, rows=8192, device="cuda", kv_dtype="fp8"):
+        out = G.sparse_fwd(w.q, w.kv, w.indices, w.sm_scale, w.kv_scale)
+        torch.cuda.synchronize()
+        ref, _ = _oracle(w, exact=False)
+        rel, cmin, finite = parity_metrics(out.float().cpu().numpy(), ref)
+        assert finite and rel <= REF_FP8_REL and cmin >= REF_FP8_COS, (w.name, rel, cmin)

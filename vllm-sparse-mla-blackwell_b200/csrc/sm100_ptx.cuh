@@ -428,4 +428,11 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, bool a_mn_ma
          (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// As idesc_bf16_f32 with f16 A/B (A and B format 0).
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N, bool a_mn_major,
+                                                     bool b_mn_major) {
+  return (1u << 4) | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
+         (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
 }  // namespace glm53

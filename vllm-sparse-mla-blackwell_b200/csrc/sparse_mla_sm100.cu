@@ -135,20 +135,24 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&b);
 }
 
-// Two e4m3 values (low byte first) -> two bf16 of value * scale. e4m3 -> f16 is
-// exact, the product is rounded once in fp32 and once to bf16, i.e. the same
-// value as bf16(float(e4m3) * scale).
-__device__ __forceinline__ uint32_t dequant2(uint32_t two, float scale) {
-  const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(two),
-                                                    __NV_E4M3);
-  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hr));
-  return pack_bf16x2(f.x * scale, f.y * scale);
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Eight e4m3 values (one 16-byte bf16 chunk) -> bf16 x scale.
-__device__ __forceinline__ uint4 dequant8(const uint2 w, float scale) {
-  return make_uint4(dequant2(w.x & 0xFFFFu, scale), dequant2(w.x >> 16, scale),
-                    dequant2(w.y & 0xFFFFu, scale), dequant2(w.y >> 16, scale));
+// fp8 KV runs the tensor-core datapath in f16: two e4m3 values (low byte
+// first) -> two f16, exactly (every e4m3 value is an f16 value). kv_scale is
+// applied in fp32 instead: to the softmax scale and to the output.
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t two) {
+  const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(two),
+                                                    __NV_E4M3);
+  return static_cast<uint32_t>(hr.x) | (static_cast<uint32_t>(hr.y) << 16);
+}
+
+// Eight e4m3 values -> one 16-byte chunk of f16.
+__device__ __forceinline__ uint4 dequant8(const uint2 w) {
+  return make_uint4(e4m3x2_to_f16x2(w.x & 0xFFFFu), e4m3x2_to_f16x2(w.x >> 16),
+                    e4m3x2_to_f16x2(w.y & 0xFFFFu), e4m3x2_to_f16x2(w.y >> 16));
 }
 
 // bf16 store of out[h0 + j][d] for j < N: neighbouring lanes (d, d ^ 1) swap
@@ -241,10 +245,35 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
     if (lane == 0) misc[kMiscWarpCount + warp] = static_cast<uint32_t>(cnt);
     if (bad) atomicOr(&g_device_status, static_cast<unsigned>(GLM53_DEV_BAD_INDEX));
   }
-  // Q (all 64 rows of the M=64 operand; rows >= H are zero) via cp.async,
-  // issued after the index loads so those are not queued behind it; its
-  // arrival is tracked by its own barrier so the KV gather never waits on it.
-  {
+  // Q (all 64 rows of the M=64 operand; rows >= H are zero), issued after
+  // the index loads so those are not queued behind it; its arrival is tracked
+  // by its own barrier so the KV gather never waits on it.
+  // bf16 KV: Q by cp.async as it is. fp8 KV (f16 datapath): Q through
+  // registers, converted to f16 with one power-of-two scale s_q per token
+  // that puts max |q * s_q| in [2^13, 2^14): exact for every bf16 value in
+  // range, never overflowing; 1 / s_q is folded into the softmax scale.
+  constexpr int kQPer = (64 * 64 + kThreads - 1) / kThreads;
+  uint4 qv[kFp8 ? kQPer : 1];
+  float s_q = 1.f;
+  if constexpr (kFp8) {
+    const __nv_bfloat16* qtok = p.q + static_cast<size_t>(token) * p.H * kDim;
+    float qmax = 0.f;
+#pragma unroll
+    for (int i = 0; i < kQPer; ++i) {
+      const int u = tid + i * kThreads;
+      const int h = u >> 6, c = u & 63;
+      qv[i] = (u < 64 * 64 && h < p.H) ? ldg_nc_v4(qtok + h * kDim + c * 8) : make_uint4(0u, 0u, 0u, 0u);
+      const uint32_t w4[4] = {qv[i].x, qv[i].y, qv[i].z, qv[i].w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w4[k]));
+        qmax = fmaxf(qmax, fmaxf(fabsf(f.x), fabsf(f.y)));
+      }
+    }
+#pragma unroll
+    for (int k = 16; k >= 1; k >>= 1) qmax = fmaxf(qmax, __shfl_xor_sync(0xFFFFFFFFu, qmax, k));
+    if (lane == 0) alpha_sm[warp] = qmax;   // alpha_sm is free until the softmax
+  } else {
     const __nv_bfloat16* qtok = p.q + static_cast<size_t>(token) * p.H * kDim;
     for (int u = tid; u < 64 * 64; u += kThreads) {
       const int h = u >> 6, c = u & 63;
@@ -254,6 +283,34 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
     cp_async_mbar_arrive_noinc(bar(kBarQFull));
   }
   __syncthreads();
+  if constexpr (kFp8) {
+    float qmax = 0.f;
+#pragma unroll
+    for (int w = 0; w < kThreads / 32; ++w) qmax = fmaxf(qmax, alpha_sm[w]);
+    int ex = 0;
+    frexpf(qmax, &ex);
+    s_q = qmax > 0.f ? ldexpf(1.f, 14 - min(max(ex, -100), 100)) : 1.f;
+#pragma unroll
+    for (int i = 0; i < kQPer; ++i) {
+      const int u = tid + i * kThreads;
+      if (u < 64 * 64) {
+        const uint32_t w4[4] = {qv[i].x, qv[i].y, qv[i].z, qv[i].w};
+        uint32_t o4[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w4[k]));
+          o4[k] = pack_f16x2(f.x * s_q, f.y * s_q);
+        }
+        sts_v4(sb + kSmQ + swz(u >> 6, u & 63), make_uint4(o4[0], o4[1], o4[2], o4[3]));
+      }
+    }
+    fence_proxy_async_smem();
+    mbar_arrive(bar(kBarQFull));
+  }
+  // fp8 KV: the tensor cores see e4m3 values and q * s_q; the softmax scale
+  // and the final normalisation take kv_scale and 1 / s_q back.
+  const float kvs = kFp8 ? p.kv_scale : 1.f;
+  const float c_soft = p.c * kvs / s_q;
 
   // pass 2: scatter the valid entries to their compacted positions
   int n_valid = 0, base = 0;
@@ -280,8 +337,10 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
   // UMMA steps. GEMM1 of tile t is 32 K-steps into S[t & 1]; GEMM2 of tile t
   // is 4 K-steps x 4 d-chunks into O^T, chunks innermost so consecutive UMMAs
   // are independent.
-  constexpr uint32_t kIdesc1 = idesc_bf16_f32(64, 64, false, false);
-  constexpr uint32_t kIdesc2 = idesc_bf16_f32(128, NH, true, false);
+  constexpr uint32_t kIdesc1 = kFp8 ? idesc_f16_f32(64, 64, false, false)
+                                    : idesc_bf16_f32(64, 64, false, false);
+  constexpr uint32_t kIdesc2 = kFp8 ? idesc_f16_f32(128, NH, true, false)
+                                    : idesc_bf16_f32(128, NH, true, false);
   constexpr int kSteps1 = kDim / 16;          // 32
   auto gemm1_step = [=](int t, int kk) {
     const uint32_t stage = sb + kSmKV + (t & 1) * kStageBytes;
@@ -301,8 +360,8 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
   // Gather rows r = r0, r0 + step, ... of tile t into its stage: bf16 rows by
   // 16-byte cp.async per lane (half a row per warp instruction; the last
   // tile's missing rows are zero-filled through src-size 0), fp8 rows by
-  // 16-byte register loads, e4m3 -> bf16 (x kv_scale) in registers and
-  // swizzled 16-byte shared stores. Then arrive on `full`: bf16 through the
+  // 8-byte register loads, e4m3 -> f16 in registers and swizzled 16-byte
+  // shared stores. Then arrive on `full`: bf16 through the
   // deferred cp.async arrive (fires once this thread's copies have landed),
   // fp8 after a proxy fence.
   auto gather_rows = [&](int t, int r0, auto step_c, uint32_t full) {
@@ -345,8 +404,8 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
       for (int j = 0; j < kPer; ++j) {
         const int r = r0 + kStep * j;
         if (r < kRows) {
-          sts_v4(stage + swz(r, lane), dequant8(buf[j][0], p.kv_scale));
-          sts_v4(stage + swz(r, lane + 32), dequant8(buf[j][1], p.kv_scale));
+          sts_v4(stage + swz(r, lane), dequant8(buf[j][0]));
+          sts_v4(stage + swz(r, lane + 32), dequant8(buf[j][1]));
         }
       }
       fence_proxy_async_smem();
@@ -366,10 +425,10 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
     // land spread out as the data arrives.
     // fp8: register-staged with one tile of prefetch: the rows of tile t + 1
     // are loaded right after tile t is stored, so their DRAM latency runs
-    // while the stage they go to is still being consumed, and dequantised
-    // (x kv_scale) at store time. (Staging bf16 the same way measured slower:
+    // while the stage they go to is still being consumed, and converted to
+    // f16 at store time. (Staging bf16 the same way measured slower:
     // its 64 KB burst of shared stores stalls the tensor core's operand reads.)
-    // Lane l owns the 16-byte bf16 chunks l and l + 32 of each of its rows: a
+    // Lane l owns the 16-byte chunks l and l + 32 of each of its rows: a
     // warp's loads cover 256 contiguous bytes and a quarter-warp's swizzled
     // stores hit 8 distinct bank groups.
     const int pw = warp - kProducerWarp0;
@@ -408,8 +467,8 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
         const int r = pw + kProducerWarps * j;
         if (r < kRows) {
           if constexpr (kFp8) {
-            sts_v4(stage + swz(r, lane), dequant8(buf[j][0], p.kv_scale));
-            sts_v4(stage + swz(r, lane + 32), dequant8(buf[j][1], p.kv_scale));
+            sts_v4(stage + swz(r, lane), dequant8(buf[j][0]));
+            sts_v4(stage + swz(r, lane + 32), dequant8(buf[j][1]));
           } else {
             sts_v4(stage + swz(r, lane), buf[j][0]);
             sts_v4(stage + swz(r, lane + 32), buf[j][1]);
@@ -502,7 +561,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const bool valid = 32 * half + j < rows;
-          v[j] = valid ? v[j] * p.c : -INFINITY;
+          v[j] = valid ? v[j] * c_soft : -INFINITY;
           mx = fmaxf(mx, v[j]);
         }
       }
@@ -545,7 +604,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
           const float p0 = exp2f(v[2 * j] - m_used);
           const float p1 = exp2f(v[2 * j + 1] - m_used);
           ps += p0 + p1;
-          packed[j] = pack_bf16x2(p0, p1);
+          packed[j] = kFp8 ? pack_f16x2(p0, p1) : pack_bf16x2(p0, p1);
         }
         l_part += ps;
         const uint32_t prow = sb + kSmP + b * kPBytes + static_cast<uint32_t>(h) * 128u;
@@ -693,7 +752,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
         scal[r * NH + tid] = e;
         L += lr * e;
       }
-      scal[8 * NH + tid] = L > 0.f ? 1.f / L : 0.f;
+      scal[8 * NH + tid] = L > 0.f ? kvs / L : 0.f;
       if (split == 0 && p.lse != nullptr && tid < p.H)
         p.lse[static_cast<size_t>(token) * p.H + tid] = L > 0.f ? log2f(L) + M : -INFINITY;
     }
@@ -757,7 +816,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
     if (warp < 4) {
       if (tid < NH) {
         const float L = l_sm[tid];
-        f_sm[tid] = L > 0.f ? 1.f / L : 0.f;
+        f_sm[tid] = L > 0.f ? kvs / L : 0.f;
         if (p.lse != nullptr && tid < p.H)
           p.lse[static_cast<size_t>(token) * p.H + tid] = L > 0.f ? log2f(L) + m_sm[tid] : -INFINITY;
       }
@@ -857,7 +916,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
         }
 #pragma unroll
         for (int r = 0; r < 4; ++r) scal[r * NH + tid] = e[r];
-        scal[4 * NH + tid] = L > 0.f ? 1.f / L : 0.f;
+        scal[4 * NH + tid] = L > 0.f ? kvs / L : 0.f;
         if (split == 0 && p.lse != nullptr && tid < p.H)
           p.lse[static_cast<size_t>(token) * p.H + tid] = L > 0.f ? log2f(L) + M : -INFINITY;
       }
@@ -920,7 +979,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
           if (lr > 0.f) L += lr * exp2f(ld_dsmem_f32(mapa_shared(m_addr, r)) - M);
         }
         const float l_own = l_sm[hh];
-        f_sm[hh] = (L > 0.f && l_own > 0.f) ? exp2f(m_sm[hh] - M) / L : 0.f;
+        f_sm[hh] = (L > 0.f && l_own > 0.f) ? kvs * exp2f(m_sm[hh] - M) / L : 0.f;
         if (split == 0 && p.lse != nullptr && hh < p.H)
           p.lse[static_cast<size_t>(token) * p.H + hh] = L > 0.f ? log2f(L) + M : -INFINITY;
       }

@@ -89,9 +89,13 @@ def quantize_fp8(x: torch.Tensor, scale: float) -> torch.Tensor:
     return (x.float() / scale).clamp(-FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn)
 
 
-def dequantize_fp8(kv8: torch.Tensor, scale: float) -> torch.Tensor:
-    """bf16(float(e4m3) * scale): the values the kernel computes with."""
-    return (kv8.float() * scale).to(torch.bfloat16)
+def dequantize_fp8(kv8: torch.Tensor, scale: float, exact: bool = False) -> torch.Tensor:
+    """The fp8 cache's values: float(e4m3) * scale in fp32 (``exact``, what
+    this repository's kernel computes with: e4m3 exactly in f16 operands,
+    the scale applied in fp32), or rounded to bf16 as the reference kernel
+    and its fp8 test do (tests/run_fp8.py:36 of the reference)."""
+    v = kv8.float() * scale
+    return v if exact else v.to(torch.bfloat16)
 
 
 def _normal_bf16(rng: np.random.Generator, shape, device) -> torch.Tensor:
