@@ -114,6 +114,33 @@ int glm53_sparse_mla_fwd_ws(const void* q, const void* kv, const int32_t* indice
                             uint64_t workspace_bytes, void* stream);
 
 /*
+ * As glm53_sparse_mla_fwd_ws, with the index list in vLLM's request-local
+ * form: topk_positions[t][k] (row stride positions_row_stride >= topk, only
+ * the first topk columns read) is a token position within request
+ * req_id_per_token[t], converted in the kernel's index compaction to the slot
+ *   block_table[req][pos / block_size] * block_stride_rows + pos % block_size
+ * (block_table row stride block_table_row_stride, max_blocks_per_req valid
+ * blocks per row; block_stride_rows = block_size for contiguous pages). A
+ * negative position, or a block past max_blocks_per_req, is masked; a slot
+ * outside [0, kv_rows) is masked and raises GLM53_DEV_BAD_INDEX. kv_rows must
+ * be below 2^31. Pointers to the three int32 arrays need 4-byte alignment.
+ * Replaces the reference backend's converter call and its narrowing copy
+ * before the op (glm53_sparse_mla/backend.py:341-348, 371-378), i.e. vLLM
+ * 0.22's triton_convert_req_index_to_global_index without a prefill
+ * workspace (v1/attention/backends/mla/sparse_utils.py:11-84 there): one
+ * launch and one [T, topk] int32 round trip through memory fewer.
+ */
+int glm53_sparse_mla_fwd_paged(const void* q, const void* kv, const int32_t* topk_positions,
+                               int64_t positions_row_stride, const int32_t* req_id_per_token,
+                               const int32_t* block_table, int64_t block_table_row_stride,
+                               int64_t max_blocks_per_req, int64_t block_size,
+                               int64_t block_stride_rows, void* out, float* lse, int64_t T,
+                               int64_t H, int64_t head_dim, int64_t kv_rows, int64_t kv_width,
+                               int64_t topk, int kv_dtype, float sm_scale, float kv_scale,
+                               int splits, void* workspace, uint64_t workspace_bytes,
+                               void* stream);
+
+/*
  * As glm53_sparse_mla_fwd_ws, for callers that cannot allocate device memory
  * when they call attention (a fixed-size memory pool, an allocator that the
  * call site cannot reach, a runtime that forbids cudaMalloc after start-up):

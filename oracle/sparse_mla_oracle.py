@@ -132,3 +132,33 @@ def e4m3_to_f32(bits: np.ndarray) -> np.ndarray:
 def dequant_fp8(bits: np.ndarray, scale: float) -> np.ndarray:
     """bf16(float(e4m3) * scale), the value the kernel places in shared memory."""
     return bf16_round(e4m3_to_f32(bits) * np.float32(scale))
+
+
+def convert_req_index_to_global(req_id, block_table, token_indices, block_size: int,
+                                block_stride_rows: int | None = None):
+    """Request-local top-k positions -> physical cache slots.
+
+    Restates the index converter the reference's backend calls before the op
+    (glm53_sparse_mla/backend.py:371-378 of the reference): vLLM 0.22.0's
+    ``triton_convert_req_index_to_global_index`` without a prefill workspace
+    (vllm/v1/attention/backends/mla/sparse_utils.py:11-84). vLLM is a
+    dependency of the reference, not part of it; this restates its published
+    rule:
+
+        out[t, k] = block_table[req_id[t], pos // block_size] * block_stride
+                    + pos % block_size,        pos = token_indices[t, k]
+
+    and -1 where pos < 0 or pos // block_size is not a valid block column
+    (0 <= block < block_table.shape[1]). ``block_stride_rows`` defaults to
+    ``block_size`` (contiguous pages), the only form that converter emits.
+    """
+    req_id = np.asarray(req_id, dtype=np.int64)
+    bt = np.asarray(block_table, dtype=np.int64)
+    pos = np.asarray(token_indices, dtype=np.int64)
+    stride = block_size if block_stride_rows is None else block_stride_rows
+    blk = np.floor_divide(pos, block_size)
+    off = pos - blk * block_size
+    ok = (pos >= 0) & (blk >= 0) & (blk < bt.shape[1])
+    rows = bt[req_id[:, None], np.where(ok, blk, 0)]
+    out = np.where(ok, rows * stride + off, -1)
+    return out.astype(np.int32)

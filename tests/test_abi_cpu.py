@@ -141,3 +141,29 @@ def test_fake_kernels_trace():
         assert out.shape == q.shape
         o2, lse = G.sparse_fwd_with_lse(q, kv, idx, 0.04)
         assert lse.shape == (4, 64) and lse.dtype == torch.float32
+
+
+PAGED_ARGS = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+              ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+              ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p] + [ctypes.c_int64] * 6 + [
+              ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_int, ctypes.c_void_p,
+              ctypes.c_uint64, ctypes.c_void_p]
+
+
+def test_paged_entry_validates_before_cuda(lib):
+    f = lib.glm53_sparse_mla_fwd_paged
+    f.argtypes = PAGED_ARGS
+
+    def call(T=4, H=64, topk=64, row_stride=64, bt_stride=8, max_blocks=8, bs=64, bstride=64,
+             kv_rows=4096):
+        return f(None, None, None, row_stride, None, None, bt_stride, max_blocks, bs, bstride,
+                 None, None, T, H, 512, kv_rows, 512, topk, 0, 0.1, 1.0, 0, None, 0, None)
+
+    assert call(H=12) == E_HEADS
+    assert call(row_stride=32) == E_RANK          # positions rows narrower than topk
+    assert call(bt_stride=4) == E_RANK            # block-table rows narrower than max_blocks
+    assert call(bs=0) == E_RANK
+    assert call(bstride=32) == E_RANK             # blocks closer than a block apart
+    assert call(kv_rows=1 << 31) == E_RANK        # slots must fit int32
+    assert call(T=0) == OK                        # nothing to do
+    assert call() == E_ALIGN                      # null pointers, still no CUDA call

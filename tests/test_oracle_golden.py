@@ -70,3 +70,17 @@ def test_fp8_dequant_helper_matches_torch():
 def test_bf16_rounding_matches_torch():
     x = (torch.randn(10000) * 3).float()
     assert np.array_equal(O.bf16_round(x.numpy()), x.to(torch.bfloat16).float().numpy())
+
+
+def test_converter_restatement_known_answers():
+    """Request-local positions -> slots, hand-checked: position p of request r
+    is block_table[r][p // 64] * 64 + p % 64, -1 for p < 0 or a block past
+    the table (vLLM 0.22.0 sparse_utils.py:11-84 semantics)."""
+    bt = np.array([[5, 2, 7], [1, 0, 3]], np.int32)
+    req = np.array([1, 0], np.int32)
+    ti = np.array([[0, 63, 64, 130, -1, 192], [0, 65, 191, 192, -5, 1]], np.int32)
+    want = np.array([[64, 127, 0, 194, -1, -1], [320, 129, 511, -1, -1, 321]], np.int32)
+    assert np.array_equal(O.convert_req_index_to_global(req, bt, ti, 64), want)
+    # a non-contiguous page layout: consecutive blocks 100 rows apart
+    got = O.convert_req_index_to_global(req, bt, ti, 64, block_stride_rows=100)
+    assert got[0, 3] == 3 * 100 + 2 and got[1, 0] == 5 * 100

@@ -111,7 +111,16 @@ enum : int { kMiscTmem = 0, kMiscWarpCount = 2, kMiscAbort = 10 };
 struct Params {
   const __nv_bfloat16* q;   // [T, H, 512]
   const void* kv;           // [R, 512] bf16 or fp8_e4m3
-  const int32_t* idx;       // [T, topk]
+  const int32_t* idx;       // [T, idx_stride], the first topk columns used
+  // Paged form (block_table != nullptr): idx holds request-local token
+  // positions, converted here to slots as block_table[req][pos / block_size]
+  // * block_stride + pos % block_size (-1 when pos < 0 or the block is past
+  // max_blocks), the conversion vLLM's index converter performs.
+  const int32_t* req_id;    // [T]
+  const int32_t* block_table;   // [requests, bt_stride]
+  long long idx_stride;
+  long long bt_stride;
+  int max_blocks, block_size, block_stride;
   __nv_bfloat16* out;       // [T, H, 512]
   float* lse;               // [T, H] or nullptr
   float* ws;                // split-merge workspace (see the merge), or nullptr
@@ -228,7 +237,10 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
   int32_t vals[8];
   uint32_t masks[8];
   if (warp < 8) {
-    const int32_t* irow = p.idx + static_cast<size_t>(token) * p.topk + k0;
+    const int32_t* irow = p.idx + static_cast<size_t>(token) * p.idx_stride + k0;
+    const int32_t* btrow =
+        p.block_table != nullptr ? p.block_table + static_cast<size_t>(p.req_id[token]) * p.bt_stride
+                                 : nullptr;
     int cnt = 0;
     bool bad = false;
 #pragma unroll
@@ -236,6 +248,15 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
       const int k = warp * per_warp + j * 32 + lane;
       int32_t v = -1;
       if (j * 32 < per_warp && k < len) v = irow[k];
+      if (btrow != nullptr && v >= 0) {
+        const int blk = v / p.block_size;
+        long long slot = -1;
+        if (blk < p.max_blocks)
+          slot = static_cast<long long>(btrow[blk]) * p.block_stride + (v - blk * p.block_size);
+        // a slot past the pool (kv_rows < 2^31 here) is reported below like
+        // any bad index
+        v = slot < 0 ? -1 : static_cast<int32_t>(slot < p.kv_rows ? slot : 0x7FFFFFFFll);
+      }
       const bool valid = v >= 0 && static_cast<long long>(v) < p.kv_rows;
       bad |= (v >= 0) && !valid;
       vals[j] = v;
@@ -1226,17 +1247,29 @@ uint64_t workspace_floats(const Plan& pl, int64_t H) {
   return workspace_floats(pl.t_main, H, pl.s_main) + workspace_floats(pl.t_tail, H, pl.s_tail);
 }
 
+// Paged index form (glm53_sparse_mla_fwd_paged): request-local positions
+// converted in the kernel.
+struct Paged {
+  const int32_t* req_id;
+  const int32_t* block_table;
+  int64_t idx_stride, bt_stride, max_blocks, block_size, block_stride;
+};
+
 // Shared body of the forward entry points. `ws == nullptr` selects the
 // distributed-shared-memory split merge; otherwise `ws` (at least
-// `ws_bytes`) is the global workspace of the L2 split merge.
+// `ws_bytes`) is the global workspace of the L2 split merge. `pg` selects the
+// paged index form.
 int launch_forward(const void* q, const void* kv, const int32_t* indices, void* out, float* lse,
                    int64_t T, int64_t H, int64_t head_dim, int64_t kv_rows, int64_t kv_width,
                    int64_t topk, int kv_dtype, float sm_scale, float kv_scale, int splits,
-                   bool use_ws, void* ws, uint64_t ws_bytes, void* stream) {
+                   bool use_ws, void* ws, uint64_t ws_bytes, void* stream,
+                   const Paged* pg = nullptr) {
   int rc = glm53_sparse_mla_check(T, H, head_dim, kv_rows, kv_width, topk, kv_dtype, splits);
   if (rc != GLM53_OK) return rc;
   if (T == 0) return GLM53_OK;
-  if (!aligned16(q) || !aligned16(kv) || !aligned16(indices) || !aligned16(out) ||
+  // the paged form reads indices with 4-byte loads at any row stride
+  const bool idx_ok = pg != nullptr ? (reinterpret_cast<uintptr_t>(indices) & 3u) == 0 : aligned16(indices);
+  if (!aligned16(q) || !aligned16(kv) || !idx_ok || !aligned16(out) ||
       q == nullptr || kv == nullptr || indices == nullptr || out == nullptr)
     return GLM53_ERR_ALIGN;
   if (lse != nullptr && (reinterpret_cast<uintptr_t>(lse) & 3u) != 0) return GLM53_ERR_ALIGN;
@@ -1261,7 +1294,15 @@ int launch_forward(const void* q, const void* kv, const int32_t* indices, void* 
     Params p;
     p.q = static_cast<const __nv_bfloat16*>(q) + t0 * q_tok;
     p.kv = kv;
-    p.idx = indices + t0 * topk;
+    const int64_t istride = pg != nullptr ? pg->idx_stride : topk;
+    p.idx = indices + t0 * istride;
+    p.idx_stride = istride;
+    p.req_id = pg != nullptr ? pg->req_id + t0 : nullptr;
+    p.block_table = pg != nullptr ? pg->block_table : nullptr;
+    p.bt_stride = pg != nullptr ? pg->bt_stride : 0;
+    p.max_blocks = pg != nullptr ? static_cast<int>(pg->max_blocks) : 0;
+    p.block_size = pg != nullptr ? static_cast<int>(pg->block_size) : 1;
+    p.block_stride = pg != nullptr ? static_cast<int>(pg->block_stride) : 1;
     p.out = static_cast<__nv_bfloat16*>(out) + t0 * q_tok;
     p.lse = lse != nullptr ? lse + t0 * H : nullptr;
     p.ws = (use_ws && s > 1) ? ws_next : nullptr;
@@ -1309,6 +1350,32 @@ extern "C" int glm53_sparse_mla_workspace_bytes(int64_t T, int64_t H, int64_t to
   if (rc != GLM53_OK) return rc;
   *bytes = 4 * workspace_floats(make_plan(T, topk, splits, dev), H);
   return GLM53_OK;
+}
+
+extern "C" int glm53_sparse_mla_fwd_paged(
+    const void* q, const void* kv, const int32_t* topk_positions, int64_t positions_row_stride,
+    const int32_t* req_id_per_token, const int32_t* block_table, int64_t block_table_row_stride,
+    int64_t max_blocks_per_req, int64_t block_size, int64_t block_stride_rows, void* out, float* lse,
+    int64_t T, int64_t H, int64_t head_dim, int64_t kv_rows, int64_t kv_width, int64_t topk,
+    int kv_dtype, float sm_scale, float kv_scale, int splits, void* workspace,
+    uint64_t workspace_bytes, void* stream) {
+  int rc = glm53_sparse_mla_check(T, H, head_dim, kv_rows, kv_width, topk, kv_dtype, splits);
+  if (rc != GLM53_OK) return rc;
+  if (positions_row_stride < topk || block_size <= 0 || block_size > (int64_t{1} << 20) ||
+      max_blocks_per_req <= 0 || max_blocks_per_req > (int64_t{1} << 30) ||
+      block_table_row_stride < max_blocks_per_req || block_stride_rows < block_size ||
+      block_stride_rows > (int64_t{1} << 24) || kv_rows > 0x7FFFFFFFll)
+    return GLM53_ERR_RANK;
+  if (T == 0) return GLM53_OK;
+  if (req_id_per_token == nullptr || block_table == nullptr ||
+      (reinterpret_cast<uintptr_t>(req_id_per_token) & 3u) != 0 ||
+      (reinterpret_cast<uintptr_t>(block_table) & 3u) != 0)
+    return GLM53_ERR_ALIGN;
+  const Paged pg{req_id_per_token, block_table, positions_row_stride, block_table_row_stride,
+                 max_blocks_per_req, block_size, block_stride_rows};
+  return launch_forward(q, kv, topk_positions, out, lse, T, H, head_dim, kv_rows, kv_width, topk,
+                        kv_dtype, sm_scale, kv_scale, splits, true, workspace, workspace_bytes,
+                        stream, &pg);
 }
 
 extern "C" int glm53_sparse_mla_fwd_ws(const void* q, const void* kv, const int32_t* indices,

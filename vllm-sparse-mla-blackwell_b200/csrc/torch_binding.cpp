@@ -88,12 +88,77 @@ void sparse_fwd_lse(torch::Tensor q, torch::Tensor kv, torch::Tensor indices, do
   run_sparse_fwd(q, kv, indices, sm_scale, kv_scale, out, lse.data_ptr<float>());
 }
 
+// Paged form: vLLM's request-local top-k positions plus req_id_per_token and
+// the block table; the kernel converts them to slots (no separate converter
+// launch, no narrowing copy: only the first `topk` columns of each row of
+// topk_positions are read, at its row stride).
+void sparse_fwd_paged(torch::Tensor q, torch::Tensor kv, torch::Tensor topk_positions,
+                      torch::Tensor req_id_per_token, torch::Tensor block_table,
+                      int64_t block_size, int64_t topk, double sm_scale, double kv_scale,
+                      torch::Tensor out, const std::optional<torch::Tensor>& lse,
+                      int64_t block_stride_rows) {
+  TORCH_CHECK(q.is_cuda() && kv.is_cuda() && topk_positions.is_cuda() && out.is_cuda() &&
+                  req_id_per_token.is_cuda() && block_table.is_cuda(),
+              "glm53_sparse_mla: all tensors must be CUDA tensors");
+  TORCH_CHECK(q.dim() == 3 && kv.dim() == 2 && topk_positions.dim() == 2,
+              "glm53_sparse_mla: expected q [T, H, 512], kv [R, 512], topk_positions [T, >= topk]");
+  TORCH_CHECK(q.scalar_type() == torch::kBFloat16, "glm53_sparse_mla: q must be bfloat16");
+  TORCH_CHECK(topk_positions.scalar_type() == torch::kInt && req_id_per_token.scalar_type() == torch::kInt &&
+                  block_table.scalar_type() == torch::kInt,
+              "glm53_sparse_mla: topk_positions, req_id_per_token and block_table must be int32");
+  TORCH_CHECK(q.is_contiguous() && kv.is_contiguous() && req_id_per_token.is_contiguous(),
+              "glm53_sparse_mla: q, kv and req_id_per_token must be contiguous");
+  TORCH_CHECK(topk_positions.stride(1) == 1 && block_table.dim() == 2 && block_table.stride(1) == 1,
+              "glm53_sparse_mla: topk_positions and block_table rows must be contiguous");
+  TORCH_CHECK(q.size(2) == kDim && kv.size(1) == kDim, "expected kv_lora_rank ", kDim,
+              " with qk_rope_head_dim 0 (NoPE)");
+  const int64_t T = q.size(0);
+  TORCH_CHECK(topk % 32 == 0 && topk > 0 && topk <= topk_positions.size(1),
+              "glm53_sparse_mla: topk must be a positive multiple of 32, at most the position columns");
+  TORCH_CHECK(topk_positions.size(0) >= T && req_id_per_token.size(0) >= T && out.sizes() == q.sizes(),
+              "glm53_sparse_mla: topk_positions and req_id_per_token need T rows, out the shape of q");
+  TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.is_contiguous(),
+              "glm53_sparse_mla: out must be a contiguous bfloat16 tensor");
+  float* lse_ptr = nullptr;
+  if (lse.has_value() && lse->defined()) {
+    TORCH_CHECK(lse->is_cuda() && lse->scalar_type() == torch::kFloat && lse->is_contiguous() &&
+                    lse->dim() == 2 && lse->size(0) == T && lse->size(1) == q.size(1),
+                "glm53_sparse_mla: lse must be a contiguous float32 CUDA tensor of shape [T, H]");
+    lse_ptr = lse->data_ptr<float>();
+  }
+  if (T == 0) return;
+  int kv_dtype = -1;
+  if (kv.scalar_type() == torch::kBFloat16) kv_dtype = GLM53_KV_BF16;
+  else if (kv.scalar_type() == torch::kFloat8_e4m3fn) kv_dtype = GLM53_KV_FP8_E4M3;
+  TORCH_CHECK(kv_dtype >= 0, "kv must be bfloat16 or float8_e4m3fn, got ", kv.scalar_type());
+  const int64_t H = q.size(1);
+  const c10::cuda::CUDAGuard guard(q.device());
+  cudaStream_t stream = c10::cuda::getCurrentCUDAStream(q.get_device()).stream();
+  uint64_t ws_bytes = 0;
+  int rc = glm53_sparse_mla_workspace_bytes(T, H, topk, /*splits=*/0, &ws_bytes);
+  TORCH_CHECK(rc == GLM53_OK, "glm53_sparse_mla: ", glm53_sparse_mla_strerror(rc));
+  torch::Tensor ws;
+  if (ws_bytes > 0)
+    ws = torch::empty({static_cast<int64_t>(ws_bytes)},
+                      torch::TensorOptions().dtype(torch::kUInt8).device(q.device()));
+  rc = glm53_sparse_mla_fwd_paged(
+      q.data_ptr(), kv.data_ptr(), topk_positions.data_ptr<int32_t>(), topk_positions.stride(0),
+      req_id_per_token.data_ptr<int32_t>(), block_table.data_ptr<int32_t>(), block_table.stride(0),
+      block_table.size(1), block_size, block_stride_rows > 0 ? block_stride_rows : block_size,
+      out.data_ptr(), lse_ptr, T, H, q.size(2), kv.size(0), kv.size(1), topk, kv_dtype,
+      static_cast<float>(sm_scale), static_cast<float>(kv_scale), /*splits=*/0,
+      ws_bytes > 0 ? ws.data_ptr() : nullptr, ws_bytes, static_cast<void*>(stream));
+  TORCH_CHECK(rc == GLM53_OK, "glm53_sparse_mla: ", glm53_sparse_mla_strerror(rc));
+}
+
 TORCH_LIBRARY(glm53_sparse_mla, m) {
   m.def("sparse_fwd(Tensor q, Tensor kv, Tensor indices, float sm_scale, float kv_scale, Tensor(a!) out) -> ()");
   m.def("sparse_fwd_lse(Tensor q, Tensor kv, Tensor indices, float sm_scale, float kv_scale, Tensor(a!) out, Tensor(b!) lse) -> ()");
+  m.def("sparse_fwd_paged(Tensor q, Tensor kv, Tensor topk_positions, Tensor req_id_per_token, Tensor block_table, int block_size, int topk, float sm_scale, float kv_scale, Tensor(a!) out, Tensor(b!)? lse=None, int block_stride_rows=0) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(glm53_sparse_mla, CUDA, m) {
   m.impl("sparse_fwd", &sparse_fwd);
   m.impl("sparse_fwd_lse", &sparse_fwd_lse);
+  m.impl("sparse_fwd_paged", &sparse_fwd_paged);
 }

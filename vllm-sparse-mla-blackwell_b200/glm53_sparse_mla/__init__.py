@@ -22,6 +22,7 @@ import torch
 __all__ = [
     "sparse_fwd",
     "sparse_fwd_with_lse",
+    "sparse_fwd_paged",
     "HEADS_PER_RANK",
     "SUPPORTED_HEADS_PER_RANK",
     "KV_LORA_RANK",
@@ -106,6 +107,34 @@ def sparse_fwd_with_lse(q, kv, indices, sm_scale, kv_scale=1.0, out=None, lse=No
     return out, lse
 
 
+def sparse_fwd_paged(q, kv, topk_positions, req_id_per_token, block_table, block_size,
+                     sm_scale, kv_scale=1.0, topk=None, out=None, lse=None,
+                     block_stride_rows=0):
+    """Sparse MLA on vLLM's request-local top-k positions.
+
+    topk_positions [T, >= topk] int32   token positions within each request
+                                        (-1 masked); only the first ``topk``
+                                        columns are read (default: all)
+    req_id_per_token [T] int32          request of each query token
+    block_table [requests, max_blocks]  int32 physical block ids
+    block_size                          tokens per cache block
+
+    The kernel maps position p of request r to the slot
+    ``block_table[r, p // block_size] * block_stride_rows + p % block_size``
+    (``block_stride_rows`` = ``block_size`` for contiguous pages, the default)
+    while it compacts the index list, as vLLM's index converter would, so
+    neither that converter nor a narrowing copy of the positions is needed.
+    Returns ``out`` (and fills ``lse`` [T, H] float32, log2 base, if given).
+    """
+    if out is None:
+        out = torch.empty_like(q)
+    k = int(topk) if topk is not None else int(topk_positions.shape[1])
+    torch.ops.glm53_sparse_mla.sparse_fwd_paged(
+        q, kv, topk_positions, req_id_per_token, block_table, int(block_size), k,
+        float(sm_scale), float(kv_scale), out, lse, int(block_stride_rows))
+    return out
+
+
 # Shape-only meta kernels so torch.compile can trace through the ops.
 @torch.library.register_fake("glm53_sparse_mla::sparse_fwd")
 def _sparse_fwd_fake(q, kv, indices, sm_scale, kv_scale, out):
@@ -119,4 +148,12 @@ def _sparse_fwd_lse_fake(q, kv, indices, sm_scale, kv_scale, out, lse):
     torch._check(q.dim() == 3 and kv.dim() == 2 and indices.dim() == 2)
     torch._check(out.shape == q.shape)
     torch._check(lse.dim() == 2 and lse.shape[0] == q.shape[0] and lse.shape[1] == q.shape[1])
+    return None
+
+
+@torch.library.register_fake("glm53_sparse_mla::sparse_fwd_paged")
+def _sparse_fwd_paged_fake(q, kv, topk_positions, req_id_per_token, block_table, block_size,
+                           topk, sm_scale, kv_scale, out, lse=None, block_stride_rows=0):
+    torch._check(q.dim() == 3 and kv.dim() == 2 and topk_positions.dim() == 2)
+    torch._check(out.shape == q.shape)
     return None

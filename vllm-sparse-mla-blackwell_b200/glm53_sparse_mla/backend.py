@@ -10,8 +10,9 @@ Same classes, methods and behaviour as the reference plugin's backend
   the builder expresses by reporting all tokens as decode tokens (the shared
   MLA layer then never enters its dense-MHA branch);
 * bf16 or plain fp8_e4m3 KV with vLLM's per-tensor scale;
-* ``AttentionCGSupport.UNIFORM_BATCH``: the op does no host sync and no
-  allocation, and its launch geometry depends only on shapes.
+* ``AttentionCGSupport.UNIFORM_BATCH``: the op does no host sync, takes its
+  split-merge workspace from the caching allocator on the current stream, and
+  its launch geometry depends only on shapes.
 
 What differs, because the kernel is built for sm_100a only:
 
@@ -21,6 +22,14 @@ What differs, because the kernel is built for sm_100a only:
   ``FLASHINFER_MLA_SPARSE_SM120``, which vLLM only lists for 12.x); the
   ``VLLM_GLM53_BACKEND_SLOT`` environment variable names another slot.
 * 64 heads per rank are supported (``SUPPORTED_HEADS_PER_RANK``).
+* ``forward_mqa`` hands the indexer's request-local positions, the block table
+  and ``req_id_per_token`` to the kernel (``sparse_fwd_paged``), which converts
+  them to slots while compacting the index list; the reference ran vLLM's
+  Triton converter and a narrowing copy first (its backend.py:341-348,
+  371-378).
+* With decode context parallelism (``dcp_world_size > 1``) ``forward_mqa``
+  returns the natural-log LSE vLLM merges the ranks' outputs with; the
+  reference returned None (its backend.py:395).
 
 Gate: ``VLLM_GLM53_CUDA_SPARSE_MLA=1``; unset, importing this module changes
 nothing.
@@ -28,7 +37,7 @@ nothing.
 
 from __future__ import annotations
 
-import inspect
+import math
 import os
 from dataclasses import dataclass
 from typing import TYPE_CHECKING, ClassVar
@@ -50,23 +59,10 @@ from vllm.v1.attention.backend import (
 )
 from vllm.v1.kv_cache_interface import AttentionSpec
 
-try:  # the converter moved between vLLM snapshots
-    from vllm.v1.attention.backends.mla.sparse_utils import (
-        triton_convert_req_index_to_global_index,
-    )
-except ImportError:  # pragma: no cover
-    from vllm.v1.attention.backends.mla.flashmla_sparse import (
-        triton_convert_req_index_to_global_index,
-    )
-
 try:  # newer vLLM: row view that knows about interleaved layer pages
     from vllm.v1.attention.backends.mla.sparse_utils import flat_kv_row_view
 except ImportError:
     flat_kv_row_view = None
-
-_CONVERTER_TAKES_STRIDE = (
-    "BLOCK_STRIDE_ROWS" in inspect.signature(triton_convert_req_index_to_global_index).parameters
-)
 
 import glm53_sparse_mla  # noqa: E402  registers torch.ops.glm53_sparse_mla.*
 
@@ -275,22 +271,20 @@ class Glm53SparseMLAImpl(MLAAttentionImpl[Glm53SparseMLAMetadata]):
             indexer.topk_indices_buffer if indexer is not None else topk_indices_buffer)
 
     def _kv_rows(self, kv_cache: torch.Tensor, attn_metadata: Glm53SparseMLAMetadata):
-        """Flat [R, 512] view of the paged cache plus converter kwargs."""
+        """Flat [R, 512] view of the paged cache and the row distance between
+        consecutive blocks (block_size for contiguous pages)."""
         head_dim = kv_cache.shape[-1]
-        kwargs = {}
         if flat_kv_row_view is not None:
             rows, stride_rows = flat_kv_row_view(kv_cache, attn_metadata.block_size)
-            if _CONVERTER_TAKES_STRIDE:
-                kwargs["BLOCK_STRIDE_ROWS"] = stride_rows
-            return rows, kwargs
-        # Without flat_kv_row_view the converter emits block * block_size +
-        # offset, a valid flat row only when the pages are contiguous.
+            return rows, int(stride_rows)
+        # Without flat_kv_row_view the pages must be contiguous for block *
+        # block_size + offset to be a flat row.
         stride0 = kv_cache.stride(0)
         assert stride0 == attn_metadata.block_size * head_dim, (
             f"paged KV block stride {stride0} != block_size * head_dim "
-            f"({attn_metadata.block_size} * {head_dim}); this vLLM's index converter "
-            f"cannot express that layout")
-        return kv_cache.view(-1, head_dim), kwargs
+            f"({attn_metadata.block_size} * {head_dim}); a flat row view of this "
+            f"layout needs vLLM's flat_kv_row_view")
+        return kv_cache.view(-1, head_dim), int(attn_metadata.block_size)
 
     @staticmethod
     def _kv_scale(layer, kv_rows: torch.Tensor) -> float:
@@ -325,25 +319,28 @@ class Glm53SparseMLAImpl(MLAAttentionImpl[Glm53SparseMLAMetadata]):
             q = torch.cat(q, dim=-1)
         n_tok = q.shape[0]
         assert self.topk_indices_buffer is not None
-        topk = self.topk_indices_buffer[:n_tok]
-        # The indexer may emit more columns than topk (rounded up to 128);
-        # narrow here rather than touching the indexer's buffer.
-        cap = int(attn_metadata.topk_tokens)
-        if topk.shape[1] > cap:
-            topk = topk[:, :cap].contiguous()
-        kv_rows, conv_kwargs = self._kv_rows(kv_c_and_k_pe_cache, attn_metadata)
-        slots = triton_convert_req_index_to_global_index(
-            attn_metadata.req_id_per_token,
-            attn_metadata.block_table,
-            topk,
-            BLOCK_SIZE=attn_metadata.block_size,
-            NUM_TOPK_TOKENS=topk.shape[1],
-            **conv_kwargs,
-        )
+        positions = self.topk_indices_buffer[:n_tok]
+        # The indexer's request-local positions go to the kernel as they are:
+        # it converts them to slots through the block table while compacting
+        # them (the conversion vLLM's index converter would launch separately)
+        # and reads only the first topk columns of each row at the buffer's
+        # row stride, so the extra columns the indexer emits (topk rounded up
+        # to 128) need no narrowing copy.
+        topk = min(int(attn_metadata.topk_tokens), positions.shape[1])
+        kv_rows, stride_rows = self._kv_rows(kv_c_and_k_pe_cache, attn_metadata)
         out = q.new_empty((n_tok, self.num_heads, self.kv_lora_rank))
-        torch.ops.glm53_sparse_mla.sparse_fwd(q, kv_rows, slots, self.softmax_scale,
-                                              self._kv_scale(layer, kv_rows), out)
-        return out, None
+        # Decode context parallelism merges the ranks' partial results by their
+        # log-sum-exp, which vLLM takes in natural-log base.
+        lse = None
+        if getattr(self, "dcp_world_size", 1) > 1:
+            lse = torch.empty((n_tok, self.num_heads), dtype=torch.float32, device=q.device)
+        glm53_sparse_mla.sparse_fwd_paged(
+            q, kv_rows, positions, attn_metadata.req_id_per_token, attn_metadata.block_table,
+            attn_metadata.block_size, self.softmax_scale, self._kv_scale(layer, kv_rows),
+            topk=topk, out=out, lse=lse, block_stride_rows=stride_rows)
+        if lse is not None:
+            lse.mul_(math.log(2.0))   # the kernel returns log2
+        return out, lse
 
 
 def _allow_plain_fp8_kv() -> None:
