@@ -327,3 +327,50 @@ def test_fp8_reference_gate(heads):
         ref, _ = _oracle(w, exact=False)
         rel, cmin, finite = parity_metrics(out.float().cpu().numpy(), ref)
         assert finite and rel <= REF_FP8_REL and cmin >= REF_FP8_COS, (w.name, rel, cmin)
+
+
+def test_cuda_graph_capture_and_replay():
+    """vLLM captures the op in CUDA graphs (UNIFORM_BATCH): capture the split
+    path (workspace from the caching allocator, programmatic dependent
+    launch) and the paged form, then replay on new inputs copied into the
+    captured buffers; each replay equals an eager call bit for bit."""
+    w = W.config_c2(device="cuda", seed=31)
+    out = torch.empty_like(w.q)
+    lse = torch.empty(w.T, w.H, device="cuda")
+    G.sparse_fwd_with_lse(w.q, w.kv, w.indices, w.sm_scale, out=out, lse=lse)   # set-up outside
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        G.sparse_fwd_with_lse(w.q, w.kv, w.indices, w.sm_scale, out=out, lse=lse)
+    for seed in (32, 33):
+        w2 = W.config_c2(device="cuda", seed=seed)
+        w.q.copy_(w2.q)
+        w.kv.copy_(w2.kv)
+        w.indices.copy_(w2.indices)
+        g.replay()
+        torch.cuda.synchronize()
+        ref_out, ref_lse = G.sparse_fwd_with_lse(w.q, w.kv, w.indices, w.sm_scale)
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref_out) and torch.equal(lse, ref_lse), seed
+    del g
+
+    # paged form: positions + block table, as the backend calls it
+    T, topk, bs = w.T, w.topk, 64
+    n_blocks = w.kv.shape[0] // bs
+    gen = torch.Generator(device="cpu").manual_seed(5)
+    bt = torch.stack([torch.randperm(n_blocks, generator=gen)[:128] for _ in range(T)]).int().cuda()
+    pos = torch.stack([torch.randperm(8192, generator=gen)[:topk] for _ in range(T)]).int().cuda()
+    req = torch.arange(T, dtype=torch.int32, device="cuda")
+    out_p = torch.empty_like(w.q)
+    G.sparse_fwd_paged(w.q, w.kv, pos, req, bt, bs, w.sm_scale, out=out_p)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        G.sparse_fwd_paged(w.q, w.kv, pos, req, bt, bs, w.sm_scale, out=out_p)
+    pos.copy_(torch.stack([torch.randperm(8192, generator=gen)[:topk] for _ in range(T)]).int())
+    g.replay()
+    torch.cuda.synchronize()
+    ref = G.sparse_fwd_paged(w.q, w.kv, pos, req, bt, bs, w.sm_scale)
+    torch.cuda.synchronize()
+    assert torch.equal(out_p, ref)
+    del g
