@@ -46,7 +46,8 @@ enum glm53_kv_dtype {
 /* Bits of the device-side status word (see glm53_sparse_mla_device_status). */
 enum glm53_device_status_bits {
   GLM53_DEV_TIMEOUT = 1u,      /* a pipeline wait gave up after its time limit   */
-  GLM53_DEV_BAD_INDEX = 2u     /* an index >= kv_rows was seen and masked out    */
+  GLM53_DEV_BAD_INDEX = 2u,    /* an index >= kv_rows was seen and masked out    */
+  GLM53_DEV_BAD_SLOT = 4u      /* cache writer: a slot past the cache was skipped */
 };
 
 /*
@@ -202,6 +203,41 @@ const char* glm53_sparse_mla_strerror(int code);
  */
 int glm53_gather_roof(const void* kv, const int32_t* indices, int64_t T, int64_t topk,
                       int64_t kv_rows, void* sink, void* stream);
+
+/*
+ * Latent KV-cache writer (the write that feeds the attention above).
+ *
+ *   kv_c          [>= T, kv_c_stride] bf16, row t = token t's 512-wide latent
+ *                 (kv_c_stride >= 512 elements; rows past T, padding for CUDA
+ *                 graphs, are ignored)
+ *   kv_cache      paged cache [num_blocks, block_size, 512] of cache_dtype,
+ *                 element (b, o, i) at b * block_stride + o * entry_stride + i
+ *                 (strides in elements; entries must not overlap)
+ *   slot_mapping  [T] int64: token t goes to block slot / block_size at offset
+ *                 slot % block_size; slot < 0 (a padded token) writes nothing;
+ *                 a slot >= num_blocks * block_size is skipped and raises
+ *                 GLM53_DEV_BAD_SLOT in glm53_concat_and_cache_status.
+ *   cache_dtype   GLM53_KV_BF16: the row is copied ("auto");
+ *                 GLM53_KV_FP8_E4M3: element = e4m3(float(x) / *scale), round
+ *                 to nearest even, saturated to +-448 ("fp8" / "fp8_e4m3").
+ *   scale         device pointer to the fp32 per-tensor scale (fp8 only; read
+ *                 on the device, so no host synchronisation).
+ *
+ * Replaces, for this path's geometry (kv_lora_rank 512, pe_dim 0), vLLM's
+ * concat_and_cache_mla (vllm 0.22.0 vllm/_custom_ops.py:2613-2623), which the
+ * reference leaves vLLM to call (its backend keeps the plain fp8 layout,
+ * glm53_sparse_mla/backend.py:398-428) through MLAAttentionImpl's
+ * do_kv_cache_update (vllm/v1/attention/backend.py:990-1010).
+ * Asynchronous on `stream`; no allocation. T == 0 is a no-op.
+ */
+int glm53_concat_and_cache(const void* kv_c, int64_t kv_c_stride, int64_t T, void* kv_cache,
+                           int cache_dtype, int64_t num_blocks, int64_t block_size,
+                           int64_t block_stride, int64_t entry_stride,
+                           const int64_t* slot_mapping, const float* scale, void* stream);
+
+/* Read (and optionally clear) the cache writer's device status word
+ * (GLM53_DEV_BAD_SLOT). Synchronises the device. Not part of the hot path. */
+int glm53_concat_and_cache_status(uint32_t* status, int clear);
 
 #ifdef __cplusplus
 }

@@ -8,10 +8,15 @@
 // same conditions, same order (T == 0 returns before the dtype / head-count
 // dispatch), raised as RuntimeError through TORCH_CHECK. The launch itself goes
 // through glm53_sparse_mla_fwd_ws on the caller's current CUDA stream.
+// `sparse_fwd_paged` takes vLLM's request-local positions directly, and
+// `concat_and_cache_mla` is the latent KV-cache write that feeds the op, with
+// the schema of vLLM's cache op of that name.
 
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
 #include <torch/all.h>
+
+#include <string>
 
 #include "glm53_sparse_mla.h"
 
@@ -151,14 +156,67 @@ void sparse_fwd_paged(torch::Tensor q, torch::Tensor kv, torch::Tensor topk_posi
   TORCH_CHECK(rc == GLM53_OK, "glm53_sparse_mla: ", glm53_sparse_mla_strerror(rc));
 }
 
+// Latent KV-cache write with the schema and argument meaning of vLLM's
+// _C_cache_ops::concat_and_cache_mla (vllm 0.22.0 vllm/_custom_ops.py:2613-2623)
+// for this path's geometry: kv_lora_rank 512, pe_dim 0. The token count is
+// slot_mapping's length (kv_c may hold more rows: padding for CUDA graphs).
+void concat_and_cache_mla(const torch::Tensor& kv_c, const torch::Tensor& k_pe,
+                          torch::Tensor& kv_cache, const torch::Tensor& slot_mapping,
+                          const std::string& kv_cache_dtype, const torch::Tensor& scale) {
+  TORCH_CHECK(kv_c.is_cuda() && kv_cache.is_cuda() && slot_mapping.is_cuda(),
+              "glm53_sparse_mla: kv_c, kv_cache and slot_mapping must be CUDA tensors");
+  TORCH_CHECK(kv_c.dim() == 2 && kv_c.size(1) == kDim && kv_c.stride(1) == 1 &&
+                  kv_c.scalar_type() == torch::kBFloat16,
+              "glm53_sparse_mla: kv_c must be bfloat16 [num_tokens, 512] with contiguous rows");
+  TORCH_CHECK(k_pe.numel() == 0, "glm53_sparse_mla: this path writes NoPE caches (pe_dim 0); got k_pe ",
+              k_pe.sizes());
+  TORCH_CHECK(kv_cache.dim() == 3 && kv_cache.size(2) == kDim && kv_cache.stride(2) == 1,
+              "glm53_sparse_mla: kv_cache must be [num_blocks, block_size, 512] (kv_lora_rank + pe_dim)");
+  TORCH_CHECK(slot_mapping.dim() == 1 && slot_mapping.scalar_type() == torch::kLong &&
+                  slot_mapping.is_contiguous(),
+              "glm53_sparse_mla: slot_mapping must be a contiguous int64 vector");
+  const int64_t T = slot_mapping.size(0);
+  TORCH_CHECK(kv_c.size(0) >= T, "glm53_sparse_mla: kv_c has fewer rows than slot_mapping");
+  TORCH_CHECK(kv_c.get_device() == kv_cache.get_device() &&
+                  slot_mapping.get_device() == kv_cache.get_device(),
+              "glm53_sparse_mla: all tensors must be on the same device");
+  int cache_dtype = -1;
+  if (kv_cache_dtype == "auto") {
+    TORCH_CHECK(kv_cache.scalar_type() == torch::kBFloat16,
+                "glm53_sparse_mla: kv_cache_dtype 'auto' needs a bfloat16 cache like kv_c");
+    cache_dtype = GLM53_KV_BF16;
+  } else if (kv_cache_dtype == "fp8" || kv_cache_dtype == "fp8_e4m3") {
+    TORCH_CHECK(kv_cache.scalar_type() == torch::kUInt8 || kv_cache.scalar_type() == torch::kFloat8_e4m3fn,
+                "glm53_sparse_mla: an fp8 cache must be uint8 or float8_e4m3fn");
+    TORCH_CHECK(scale.is_cuda() && scale.scalar_type() == torch::kFloat && scale.numel() >= 1 &&
+                    scale.get_device() == kv_cache.get_device(),
+                "glm53_sparse_mla: scale must be a float32 CUDA tensor on the cache's device");
+    cache_dtype = GLM53_KV_FP8_E4M3;
+  } else {
+    TORCH_CHECK(false, "glm53_sparse_mla: unsupported kv_cache_dtype '", kv_cache_dtype,
+                "' (this path writes 'auto' bf16 or 'fp8' / 'fp8_e4m3')");
+  }
+  if (T == 0) return;
+  const c10::cuda::CUDAGuard guard(kv_cache.device());
+  cudaStream_t stream = c10::cuda::getCurrentCUDAStream(kv_cache.get_device()).stream();
+  const int rc = glm53_concat_and_cache(
+      kv_c.data_ptr(), kv_c.stride(0), T, kv_cache.data_ptr(), cache_dtype, kv_cache.size(0),
+      kv_cache.size(1), kv_cache.stride(0), kv_cache.stride(1), slot_mapping.data_ptr<int64_t>(),
+      cache_dtype == GLM53_KV_FP8_E4M3 ? scale.data_ptr<float>() : nullptr,
+      static_cast<void*>(stream));
+  TORCH_CHECK(rc == GLM53_OK, "glm53_sparse_mla: ", glm53_sparse_mla_strerror(rc));
+}
+
 TORCH_LIBRARY(glm53_sparse_mla, m) {
   m.def("sparse_fwd(Tensor q, Tensor kv, Tensor indices, float sm_scale, float kv_scale, Tensor(a!) out) -> ()");
   m.def("sparse_fwd_lse(Tensor q, Tensor kv, Tensor indices, float sm_scale, float kv_scale, Tensor(a!) out, Tensor(b!) lse) -> ()");
   m.def("sparse_fwd_paged(Tensor q, Tensor kv, Tensor topk_positions, Tensor req_id_per_token, Tensor block_table, int block_size, int topk, float sm_scale, float kv_scale, Tensor(a!) out, Tensor(b!)? lse=None, int block_stride_rows=0) -> ()");
+  m.def("concat_and_cache_mla(Tensor kv_c, Tensor k_pe, Tensor(a!) kv_cache, Tensor slot_mapping, str kv_cache_dtype, Tensor scale) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(glm53_sparse_mla, CUDA, m) {
   m.impl("sparse_fwd", &sparse_fwd);
   m.impl("sparse_fwd_lse", &sparse_fwd_lse);
   m.impl("sparse_fwd_paged", &sparse_fwd_paged);
+  m.impl("concat_and_cache_mla", &concat_and_cache_mla);
 }

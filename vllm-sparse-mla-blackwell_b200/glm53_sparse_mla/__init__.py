@@ -23,6 +23,7 @@ __all__ = [
     "sparse_fwd",
     "sparse_fwd_with_lse",
     "sparse_fwd_paged",
+    "concat_and_cache_mla",
     "HEADS_PER_RANK",
     "SUPPORTED_HEADS_PER_RANK",
     "KV_LORA_RANK",
@@ -135,6 +136,23 @@ def sparse_fwd_paged(q, kv, topk_positions, req_id_per_token, block_table, block
     return out
 
 
+def concat_and_cache_mla(kv_c, k_pe, kv_cache, slot_mapping, kv_cache_dtype, scale):
+    """Write new tokens' latent rows into the paged cache the op reads.
+
+    kv_c [N, 512] bf16 (rows may be strided), k_pe [N, 0] (NoPE), kv_cache
+    [num_blocks, block_size, 512] (bf16 for ``"auto"``; uint8 or
+    float8_e4m3fn for ``"fp8"`` / ``"fp8_e4m3"``), slot_mapping [T] int64
+    (T <= N; slot < 0 = padded token, skipped), scale: float32 CUDA tensor,
+    the per-tensor fp8 scale (element = e4m3(x / scale), saturating).
+
+    Same argument list and meaning as vLLM's ``ops.concat_and_cache_mla``
+    (vllm 0.22.0 vllm/_custom_ops.py:2613-2623), which the reference leaves
+    vLLM to call; here it runs this package's sm_100a kernel.
+    """
+    torch.ops.glm53_sparse_mla.concat_and_cache_mla(kv_c, k_pe, kv_cache, slot_mapping,
+                                                    str(kv_cache_dtype), scale)
+
+
 # Shape-only meta kernels so torch.compile can trace through the ops.
 @torch.library.register_fake("glm53_sparse_mla::sparse_fwd")
 def _sparse_fwd_fake(q, kv, indices, sm_scale, kv_scale, out):
@@ -156,4 +174,10 @@ def _sparse_fwd_paged_fake(q, kv, topk_positions, req_id_per_token, block_table,
                            topk, sm_scale, kv_scale, out, lse=None, block_stride_rows=0):
     torch._check(q.dim() == 3 and kv.dim() == 2 and topk_positions.dim() == 2)
     torch._check(out.shape == q.shape)
+    return None
+
+
+@torch.library.register_fake("glm53_sparse_mla::concat_and_cache_mla")
+def _concat_and_cache_mla_fake(kv_c, k_pe, kv_cache, slot_mapping, kv_cache_dtype, scale):
+    torch._check(kv_c.dim() == 2 and kv_cache.dim() == 3 and slot_mapping.dim() == 1)
     return None

@@ -30,6 +30,9 @@ What differs, because the kernel is built for sm_100a only:
 * With decode context parallelism (``dcp_world_size > 1``) ``forward_mqa``
   returns the natural-log LSE vLLM merges the ranks' outputs with; the
   reference returned None (its backend.py:395).
+* ``do_kv_cache_update`` writes the latent cache with this package's sm_100a
+  writer (``concat_and_cache_mla``); the reference inherited vLLM's, which
+  calls vLLM's compiled op of that name.
 
 Gate: ``VLLM_GLM53_CUDA_SPARSE_MLA=1``; unset, importing this module changes
 nothing.
@@ -296,6 +299,21 @@ class Glm53SparseMLAImpl(MLAAttentionImpl[Glm53SparseMLAMetadata]):
         if s is None:
             return 1.0
         return float(s.item()) if torch.is_tensor(s) else float(s)
+
+    def do_kv_cache_update(self, kv_c_normed: torch.Tensor, k_pe: torch.Tensor,
+                           kv_cache: torch.Tensor, slot_mapping: torch.Tensor,
+                           kv_cache_dtype: str, k_scale: torch.Tensor) -> None:
+        """Write the step's new latent rows into the paged cache with this
+        package's sm_100a writer: the same write, with the same arguments, as
+        MLAAttentionImpl's default, which calls vLLM's concat_and_cache_mla
+        (vllm 0.22.0 vllm/v1/attention/backend.py:990-1010); bf16 for
+        ``auto``, plain e4m3(x / k_scale) for ``fp8`` / ``fp8_e4m3``."""
+        if kv_cache.numel() == 0:
+            return
+        if k_pe.dim() == 3:
+            k_pe = k_pe.squeeze(1)
+        glm53_sparse_mla.concat_and_cache_mla(kv_c_normed, k_pe, kv_cache, slot_mapping.flatten(),
+                                              kv_cache_dtype, k_scale)
 
     def forward_mha(self, q, kv_c_normed, k_pe, kv_c_and_k_pe_cache, attn_metadata, k_scale,
                     output) -> None:

@@ -42,6 +42,8 @@ NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "--expt-relaxed-constexpr",
               "-Xcompiler", "-fPIC", "-Xptxas", "--warn-on-spills"]
 
 LIB_NAME = "libglm53_sparse_mla.so"
+# attention kernel + host launcher; latent KV-cache writer
+KERNEL_SOURCES = ["sparse_mla_sm100.cu", "kv_cache_writer_sm100.cu"]
 OP_NAME = "_C.so"
 
 
@@ -65,12 +67,12 @@ def _newer(target: str, deps: list[str]) -> bool:
 
 def build_kernel_lib(force: bool = False, verbose: bool = False) -> str:
     inc = _find_include_dir()
-    src = os.path.join(CSRC, "sparse_mla_sm100.cu")
-    deps = [src, os.path.join(CSRC, "sm100_ptx.cuh"), os.path.join(inc, "glm53_sparse_mla.h")]
+    srcs = [os.path.join(CSRC, f) for f in KERNEL_SOURCES]
+    deps = srcs + [os.path.join(CSRC, "sm100_ptx.cuh"), os.path.join(inc, "glm53_sparse_mla.h")]
     out = os.path.join(PKG_DIR, LIB_NAME)
     if force or _newer(out, deps):
         tmp = out + ".tmp"
-        _run([NVCC, *GENCODE, *NVCC_FLAGS, "-I", inc, "-I", CSRC, "-shared", src, "-o", tmp],
+        _run([NVCC, *GENCODE, *NVCC_FLAGS, "-I", inc, "-I", CSRC, "-shared", *srcs, "-o", tmp],
              verbose)
         os.replace(tmp, out)
     return out
