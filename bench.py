@@ -35,6 +35,11 @@ heads of one batch across ranks (tensor-parallel heads, strong scaling), with
 
 --impl reference times the reference's CPU implementation of the path (the
 oracle port) on the host cores instead, on rank 0 only.
+
+--op cache_write measures the latent KV-cache writer instead (the write that
+feeds the attention): --tokens new tokens per step (default 8192, a
+chunked-prefill step) into a 524288-slot paged cache, --kv fp8 (default bf16)
+for the plain fp8 cache, same JSON line with its own metric and roofline.
 """
 
 from __future__ import annotations
@@ -66,6 +71,10 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--op", choices=["attention", "cache_write"], default="attention",
+                    help="attention (the headline) or the latent KV-cache writer")
+    ap.add_argument("--tokens", type=int, default=8192,
+                    help="cache_write: new tokens per step (a chunked-prefill step)")
     ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5"], default="c2")
     ap.add_argument("--heads", type=int, default=0, help="heads per launch (0 = workload's)")
     ap.add_argument("--kv", choices=["bf16", "fp8"], default="bf16", help="C5 KV dtype")
@@ -361,6 +370,176 @@ def run_ours(args, dist: Dist):
     dist.close()
 
 
+# ---------------------------------------------------------------------------
+# the latent KV-cache writer (--op cache_write)
+# ---------------------------------------------------------------------------
+CACHE_POOL_SLOTS = 524288        # C4's pool: 8192 blocks of 64
+CACHE_BLOCK = 64
+CW_UNIT = "cache-tokens/s"
+
+
+def cache_write_sets(args, device, n_sets: int, seed0: int = 300):
+    """n_sets independent steps: kv_c [tokens, 512] bf16 and distinct slots."""
+    g = torch.Generator(device="cpu")
+    sets = []
+    for s in range(n_sets):
+        g.manual_seed(seed0 + s)
+        kv_c = torch.randn((args.tokens, 512), generator=g).to(torch.bfloat16)
+        slots = torch.randperm(CACHE_POOL_SLOTS, generator=g)[:args.tokens].to(torch.int64)
+        sets.append((kv_c.to(device), slots.to(device)))
+    return sets
+
+
+def cache_write_bytes(tokens: int, fp8: bool) -> int:
+    """Algorithmic bytes per launch: the bf16 row read, the cache entry
+    written, the slot read."""
+    return tokens * (1024 + (512 if fp8 else 1024) + 8)
+
+
+def cache_write_desc(args, fp8: bool) -> dict:
+    return {"workload": f"latent KV-cache write: {args.tokens} new tokens per step into a "
+                        f"{CACHE_POOL_SLOTS}-slot paged {'fp8_e4m3' if fp8 else 'bf16'} cache "
+                        f"(block {CACHE_BLOCK}), random distinct slots",
+            "tokens_per_step": args.tokens, "kv_dtype": "fp8_e4m3" if fp8 else "bf16"}
+
+
+def run_cache_write(args, dist: Dist):
+    torch.cuda.set_device(dist.local)
+    device = torch.device("cuda", dist.local)
+    dist.init("nccl")
+    import glm53_sparse_mla as G
+    fp8 = args.kv == "fp8"
+    dtype = "fp8" if fp8 else "auto"
+    cache = torch.zeros((CACHE_POOL_SLOTS // CACHE_BLOCK, CACHE_BLOCK, 512),
+                        dtype=torch.uint8 if fp8 else torch.bfloat16, device=device)
+    scale = torch.tensor([0.05 if fp8 else 1.0], dtype=torch.float32, device=device)
+    sets = cache_write_sets(args, device, max(1, args.sets), 300 + 1000 * dist.rank)
+    empty_pe = sets[0][0][:, :0]
+
+    def step(k):
+        kv_c, slots = sets[k % len(sets)]
+        G.concat_and_cache_mla(kv_c, empty_pe, cache, slots, dtype, scale)
+
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        for k in range(max(args.warmup, 3)):
+            step(k)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for k in range(args.steps):
+            step(k)
+    torch.cuda.synchronize()
+    graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dist.local, enabled=not args.no_clocks) as clk:
+        t_end = time.time() + (0.0 if args.no_clocks else 0.5)
+        while time.time() < t_end:
+            graph.replay()
+            torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            graph.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+    ms_local = e0.elapsed_time(e1)
+    ms_step = dist.max(ms_local, device) / args.steps
+    value = args.tokens * dist.world / (ms_step / 1e3)
+    alg = cache_write_bytes(args.tokens, fp8)
+    hbm_peak, _, peak_kind = measured_peaks()
+    achieved = alg / (ms_local / args.steps / 1e3) / 1e9
+    m = None
+    prof = os.path.join(REPO, "profiles", f"kv_cache_writer_{args.kv}.md")
+    if os.path.exists(prof):
+        m = re.search(r"traffic_bytes_per_launch:\s*([0-9]+)", open(prof).read())
+    roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+            "frac": round(achieved / hbm_peak, 4), "peak_source": peak_kind,
+            "traffic": int(m.group(1)) if m else None, "algorithmic_bytes_per_launch": alg}
+    del graph
+    torch.cuda.synchronize()
+    e2e = None
+    if not args.no_e2e:
+        # host buffers: each step copies kv_c and slots in, writes, and reads
+        # the written entries' first block back
+        hk = [kv.cpu().pin_memory() for kv, _ in sets]
+        hs = [sl.cpu().pin_memory() for _, sl in sets]
+        dk = [torch.empty_like(kv) for kv, _ in sets]
+        ds = [torch.empty_like(sl) for _, sl in sets]
+        back = torch.empty(cache[0].shape, dtype=cache.dtype).pin_memory()
+
+        def e2e_step(k):
+            j = k % len(sets)
+            dk[j].copy_(hk[j], non_blocking=True)
+            ds[j].copy_(hs[j], non_blocking=True)
+            G.concat_and_cache_mla(dk[j], empty_pe, cache, ds[j], dtype, scale)
+            back.copy_(cache[0], non_blocking=True)
+
+        for k in range(max(args.warmup, 3)):
+            e2e_step(k)
+        torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record()
+        for k in range(args.steps):
+            e2e_step(k)
+        f1.record()
+        torch.cuda.synchronize()
+        ms_e = dist.max(f0.elapsed_time(f1), device) / args.steps
+        e2e = {"value": round(args.tokens * dist.world / (ms_e / 1e3), 1), "unit": CW_UNIT,
+               "h2d_bytes_per_step": args.tokens * (1024 + 8),
+               "d2h_bytes_per_step": int(back.numel() * back.element_size()),
+               "ms_per_step": round(ms_e, 5),
+               "path": "glm53_sparse_mla.concat_and_cache_mla (torch op -> C ABI), pinned host "
+                       "buffers; one cache block read back"}
+    cpu = None
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        cpu = cache_write_cpu(sets[0], fp8, args.cpu_seconds)
+    if dist.rank == 0:
+        cfg = cache_write_desc(args, fp8)
+        cfg.update({"parallelism": f"dp{dist.world}",
+                    "l2": f"{len(sets)} rotating input sets; writes land in random slots of a "
+                          f"{cache.numel() * cache.element_size() / 1e6:.0f} MB cache",
+                    "timing": "K steps in one CUDA graph, CUDA events, max over ranks"})
+        line = {"metric": f"latent KV-cache writes ({args.kv}), {CW_UNIT}", "value": round(value, 1),
+                "unit": CW_UNIT, "n_gpus": dist.world, "steps": args.steps,
+                "warmup": max(args.warmup, 3), "ms_per_step": round(ms_step, 5),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "bf16->fp8_e4m3" if fp8 else "bf16",
+                "data": "synthetic (seeded)", "config": cfg, "roofline": roof,
+                "cpu_baseline": cpu, "e2e": e2e,
+                "gpu_launches": args.steps + (args.steps if e2e else 0),
+                "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+    dist.close()
+
+
+def cache_write_cpu(one_set, fp8: bool, seconds: float):
+    """The oracle's cache write timed on this host over a sample of the step."""
+    from oracle import cache_writer_oracle as CW
+    kv_c, slots = one_set
+    bits = kv_c.cpu().view(torch.uint16).numpy()
+    sl = slots.cpu().numpy()
+    n = min(len(sl), 1024)
+    cache = np.zeros((CACHE_POOL_SLOTS // CACHE_BLOCK, CACHE_BLOCK, 512),
+                     np.uint8 if fp8 else np.uint16)
+    done, t0 = 0, time.perf_counter()
+    while True:
+        CW.concat_and_cache_mla(bits[:n], cache, sl[:n], "fp8" if fp8 else "auto", 0.05,
+                                inplace=True)
+        done += n
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(done / dt, 2), "unit": CW_UNIT, "cores": 1, "kind": "port",
+            "sample": f"{done} tokens in batches of {n}, numpy oracle (restates vLLM's "
+                      f"concat_and_cache_mla), {dt:.1f} s"}
+
+
 def run_e2e(args, G, sets, device, dist: Dist):
     n = len(sets)
     q_h = [w.q.cpu().pin_memory() for w in sets]
@@ -492,10 +671,33 @@ def run_reference(args, dist: Dist):
     print(json.dumps(line), flush=True)
 
 
+def run_cache_write_reference(args, dist: Dist):
+    """Reference arm of --op cache_write: the oracle's restatement of vLLM's
+    write timed on the host, rank 0 only."""
+    if dist.rank != 0:
+        return
+    fp8 = args.kv == "fp8"
+    sets = cache_write_sets(args, "cpu", 1)
+    cpu = cache_write_cpu(sets[0], fp8, max(1.0, min(args.cpu_seconds, 30.0)))
+    line = {"impl": "reference", "metric": f"latent KV-cache writes ({args.kv}), {CW_UNIT}",
+            "value": cpu["value"], "unit": CW_UNIT, "n_gpus": dist.world, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+            "config": cache_write_desc(args, fp8), "cpu_baseline": cpu,
+            "e2e": {"value": cpu["value"], "unit": CW_UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     dist = Dist(args.gpus)
-    if args.impl == "reference":
+    if args.op == "cache_write":
+        if args.impl == "reference":
+            run_cache_write_reference(args, dist)
+        else:
+            run_cache_write(args, dist)
+    elif args.impl == "reference":
         run_reference(args, dist)
     else:
         run_ours(args, dist)

@@ -59,20 +59,22 @@ def f32_to_e4m3_satfinite(x: np.ndarray) -> np.ndarray:
 
 
 def quantize_row_e4m3(row_bf16_bits: np.ndarray, scale: float) -> np.ndarray:
-    """One cache entry of the fp8 path: e4m3(float(x) / scale) per element."""
+    """Cache entries of the fp8 path: e4m3(float(x) / scale) per element."""
     v = bf16_to_f32(row_bf16_bits)
     q = (v / np.float32(scale)).astype(np.float32)              # IEEE fp32 division
     return f32_to_e4m3_satfinite(q)
 
 
 def concat_and_cache_mla(kv_c_bits: np.ndarray, cache: np.ndarray, slot_mapping: np.ndarray,
-                         kv_cache_dtype: str, scale: float = 1.0) -> np.ndarray:
-    """Returns the cache after the write, as a new array.
+                         kv_cache_dtype: str, scale: float = 1.0,
+                         inplace: bool = False) -> np.ndarray:
+    """Returns the cache after the write (a new array unless ``inplace``).
 
     kv_c_bits: uint16 bf16 bit patterns [N >= T, 512]; cache: uint16 (auto) or
     uint8 (fp8) [num_blocks, block_size, 512]; slot_mapping: int [T].
     """
-    cache = np.array(cache, copy=True)
+    if not inplace:
+        cache = np.array(cache, copy=True)
     nb, bs, width = cache.shape
     assert width == KV_WIDTH and kv_c_bits.shape[1] == KV_WIDTH
     slots = np.asarray(slot_mapping, dtype=np.int64)
@@ -80,10 +82,8 @@ def concat_and_cache_mla(kv_c_bits: np.ndarray, cache: np.ndarray, slot_mapping:
     fp8 = kv_cache_dtype in ("fp8", "fp8_e4m3")
     if not fp8 and kv_cache_dtype != "auto":
         raise ValueError(f"kv_cache_dtype {kv_cache_dtype!r} is not written by this path")
-    for t, s in enumerate(slots):
-        if s < 0:
-            continue
-        blk, off = divmod(int(s), bs)
-        row = kv_c_bits[t]
-        cache[blk, off] = quantize_row_e4m3(row, scale) if fp8 else row
+    t = np.nonzero(slots >= 0)[0]              # padded tokens write nothing
+    blk, off = np.divmod(slots[t], bs)
+    rows = kv_c_bits[t]
+    cache[blk, off] = quantize_row_e4m3(rows, scale) if fp8 else rows
     return cache

@@ -83,6 +83,37 @@ def test_matches_oracle(dtype, scale, T, kv_stride, page_pad):
     assert np.array_equal(got[:, bs:], want_buf[:, bs:])   # page padding untouched
 
 
+SCALES = [1.0, 0.05, 3.7, 1.0 / 3.0, 2.0 ** -7, 448.0 / 65504.0, 1e-3, 123.456, 0.999, 1.001,
+          -0.5] + list(np.exp(np.random.default_rng(5).uniform(np.log(1e-4), np.log(1e4), 30)))
+
+
+def _all_bf16():
+    """Every bf16 bit pattern once: 128 rows x 512."""
+    return torch.arange(65536, dtype=torch.int32).to(torch.int16).view(torch.bfloat16) \
+        .reshape(128, 512).to(DEV)
+
+
+def test_fp8_every_bf16_value_every_scale():
+    """The division by the scale (reciprocal + FMA correction) and the e4m3
+    conversion, over all 65536 bf16 inputs at each scale: bytes equal the
+    oracle's IEEE-division result; NaN inputs give an e4m3 NaN."""
+    kv_c = _all_bf16()
+    bits = _bits(kv_c)
+    nan = np.isnan(O.bf16_to_f32(bits))
+    slots = torch.arange(128, dtype=torch.int64, device=DEV)
+    for scale in SCALES:
+        cache = torch.zeros((2, 64, 512), dtype=torch.uint8, device=DEV)
+        G.concat_and_cache_mla(kv_c, kv_c[:, :0], cache, slots, "fp8",
+                               torch.tensor([scale], dtype=torch.float32, device=DEV))
+        got = _bits(cache).reshape(128, 512)
+        want = CW.concat_and_cache_mla(bits, np.zeros((2, 64, 512), np.uint8),
+                                       np.arange(128), "fp8", float(np.float32(scale)))
+        want = want.reshape(128, 512)
+        bad = (got != want) & ~nan
+        assert not bad.any(), (scale, int(bad.sum()), bits[bad][:8], got[bad][:8], want[bad][:8])
+        assert np.all((got[nan] & 0x7F) == 0x7F)
+
+
 def test_empty_batch_is_a_no_op():
     cache, buf = _cache(2, 16, "fp8", 0, seed=1)
     before = _bits(buf).copy()
@@ -112,6 +143,18 @@ def test_matches_vllm_op():
         ops.concat_and_cache_mla(kv_c, k_pe, theirs, slots, dtype, s)
         torch.cuda.synchronize()
         assert torch.equal(ours.view(torch.uint8), theirs.view(torch.uint8)), (dtype, scale)
+    # every bf16 value (NaN and inf included) at every test scale
+    allv = _all_bf16()
+    slots = torch.arange(128, dtype=torch.int64, device=DEV)
+    pe = torch.empty((128, 0), dtype=torch.bfloat16, device=DEV)
+    for scale in SCALES:
+        ours = torch.zeros((2, 64, 512), dtype=torch.uint8, device=DEV)
+        theirs = ours.clone()
+        s = torch.tensor([scale], dtype=torch.float32, device=DEV)
+        G.concat_and_cache_mla(allv, pe, ours, slots, "fp8", s)
+        ops.concat_and_cache_mla(allv, pe, theirs, slots, "fp8", s)
+        torch.cuda.synchronize()
+        assert torch.equal(ours, theirs), scale
 
 
 def test_slot_past_cache_is_skipped_and_reported():

@@ -56,16 +56,39 @@ __device__ __forceinline__ uint4 ldg_stream_v4(const void* p) {
   return v;
 }
 
+// x / s rounded to nearest fp32, from r = RN(1 / s) with one FMA correction:
+// q = RN(x * r), rem = x - s * q (exact through the FMA), RN(q + rem * r) is
+// the correctly rounded quotient when nothing overflows or underflows
+// (Markstein's theorem on FMA division: P. Markstein, IBM J. Res. Dev. 34(1),
+// 1990; also in Muller et al., Handbook of Floating-Point Arithmetic).
+// Outside that range the e4m3 result does not depend on the last bit:
+// |q| >= 512 saturates to 448 either way (the correction is skipped there, so
+// an x / s beyond fp32 range cannot become inf - inf), and quotients far below
+// the smallest e4m3 subnormal round to 0. A zero result keeps q's sign, as
+// the division would. The caller falls back to the division itself when r is
+// not finite (s zero, subnormal or not finite).
+__device__ __forceinline__ float div_by_scale(const float x, const float s, const float r) {
+  const float q = x * r;
+  if (!(fabsf(q) < 512.f)) return q;
+  const float c = fmaf(fmaf(-s, q, x), r, q);
+  return c == 0.f ? q : c;
+}
+
 // Eight bf16 -> eight e4m3 (byte j = element j): fp32 division by the scale,
 // then the hardware float -> e4m3 conversion with saturation.
-__device__ __forceinline__ uint2 quantize8(const uint4 w, const float s) {
+__device__ __forceinline__ uint2 quantize8(const uint4 w, const float s, const float r) {
   const uint32_t in[4] = {w.x, w.y, w.z, w.w};
   uint32_t out[2] = {0u, 0u};
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&in[k]));
-    f.x = __fdiv_rn(f.x, s);
-    f.y = __fdiv_rn(f.y, s);
+    if (isfinite(r)) {
+      f.x = div_by_scale(f.x, s, r);
+      f.y = div_by_scale(f.y, s, r);
+    } else {
+      f.x = __fdiv_rn(f.x, s);
+      f.y = __fdiv_rn(f.y, s);
+    }
     const uint32_t q = __nv_cvt_float2_to_fp8x2(f, __NV_SATFINITE, __NV_E4M3);
     out[k >> 1] |= (q & 0xFFFFu) << (16 * (k & 1));
   }
@@ -90,9 +113,10 @@ __global__ void __launch_bounds__(32 * kWarpsPerBlock) concat_and_cache_kernel(c
   const uint4 b = ldg_stream_v4(src + 256 + 8 * lane);
   if constexpr (kFp8) {
     const float s = *p.scale;
+    const float r = __frcp_rn(s);
     uint8_t* dst = p.cache + entry;
-    *reinterpret_cast<uint2*>(dst + 8 * lane) = quantize8(a, s);
-    *reinterpret_cast<uint2*>(dst + 256 + 8 * lane) = quantize8(b, s);
+    *reinterpret_cast<uint2*>(dst + 8 * lane) = quantize8(a, s, r);
+    *reinterpret_cast<uint2*>(dst + 256 + 8 * lane) = quantize8(b, s, r);
   } else {
     __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.cache) + entry;
     *reinterpret_cast<uint4*>(dst + 8 * lane) = a;
