@@ -239,6 +239,39 @@ int glm53_concat_and_cache(const void* kv_c, int64_t kv_c_stride, int64_t T, voi
  * (GLM53_DEV_BAD_SLOT). Synchronises the device. Not part of the hot path. */
 int glm53_concat_and_cache_status(uint32_t* status, int clear);
 
+/*
+ * Per-row top-k of the sparse-attention indexer's logits: fills the
+ * request-local top-k positions the attention consumes.
+ *
+ *   logits      [num_rows, stride0] fp32 (stride1 must be 1)
+ *   row r covers logits[r, start, end):
+ *     decode  (seq_lens != NULL, row_starts = row_ends = NULL):
+ *             start = 0, end = seq_lens[r / next_n] - next_n + r % next_n + 1
+ *     prefill (seq_lens == NULL): start = row_starts[r], end = row_ends[r]
+ *   out         [num_rows, out_stride] int32, the first topk columns written:
+ *               len = end - start <= topk: 0, 1, ..., len - 1, then -1;
+ *               otherwise the positions (relative to start) of the topk
+ *               largest values in no particular order (IEEE order, +NaN above
+ *               +inf; which of several values equal to the k-th largest are
+ *               taken is unspecified).
+ *
+ * Replaces vLLM's top_k_per_row_decode / top_k_per_row_prefill (vllm 0.22.0
+ * vllm/_custom_ops.py:2799-2840), which vLLM's sparse-attention indexer calls
+ * to fill the topk_indices_buffer the reference's backend reads
+ * (glm53_sparse_mla/backend.py:310-314 of the reference). 1 <= topk <= 16384.
+ * The first call on a device sets the kernel's shared-memory size; make it
+ * before any stream capture. Asynchronous on `stream`; no allocation.
+ */
+int glm53_topk_per_row(const float* logits, int64_t num_rows, int64_t stride0, int64_t stride1,
+                       const int32_t* seq_lens, int next_n, const int32_t* row_starts,
+                       const int32_t* row_ends, int32_t* out, int64_t out_stride, int topk,
+                       void* stream);
+
+/* Read (and optionally clear) the top-k kernel's device status word
+ * (GLM53_DEV_TIMEOUT: a row load gave up after its time limit).
+ * Synchronises the device. Not part of the hot path. */
+int glm53_topk_status(uint32_t* status, int clear);
+
 #ifdef __cplusplus
 }
 #endif

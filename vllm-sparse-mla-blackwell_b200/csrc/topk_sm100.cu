@@ -1,0 +1,507 @@
+// Per-row top-k of the indexer's logits, sm_100a: the step that turns the
+// sparse-attention indexer's scores into the request-local top-k positions the
+// attention consumes (vLLM's topk_indices_buffer). Same contract as vLLM
+// 0.22.0's top_k_per_row_decode / top_k_per_row_prefill (vllm/_custom_ops.py:
+// 2799-2840, called from vllm/model_executor/layers/sparse_attn_indexer.py:
+// 247-256 and 351-360):
+//
+//   row r covers logits[r, start, end):
+//     decode:  start = 0, end = seq_lens[r / next_n] - next_n + r % next_n + 1
+//     prefill: start = row_starts[r], end = row_ends[r]
+//   len = end - start <= k: out[r] = 0, 1, ..., len - 1, then -1 up to k;
+//   otherwise out[r] = the positions (relative to start) of the k largest
+//   values, in no particular order; among values equal to the k-th largest,
+//   which ones are taken is unspecified. Values compare by IEEE order with
+//   +NaN above +inf.
+//
+// Design: one CTA of 512 threads per row, radix selection on order-preserving
+// 32-bit keys. The row goes through shared memory in chunks of up to 36K
+// values, each brought in by one bulk copy (plus plain loads for its ragged
+// ends); a row that fits in one chunk is loaded once.
+//   1. Histogram of the top 11 key bits over the row (four copies, so shared
+//      atomics collide across four warps at most); a block-wide suffix scan
+//      finds the bin d0 holding the k-th largest key.
+//   2. One pass over the row writes every position whose top bits are above
+//      d0 and gathers the keys in bin d0 (typically a few percent of the row)
+//      with their positions as candidates; each thread counts its strided
+//      share, and a block scan of the counts places every write without
+//      atomics or per-element warp votes.
+//   3. The remaining 21 bits are resolved on the candidates alone (5-, 8- and
+//      8-bit digits, stopping as soon as a whole bin is taken), and the
+//      candidates above the threshold plus the first of those equal to it
+//      are written.
+// A row whose bin d0 holds more than kCand keys (heavy ties) resolves the
+// remaining bits with passes over the whole row instead.
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "glm53_sparse_mla.h"
+
+namespace glm53 {
+namespace topk {
+
+constexpr int kThreads = 512;
+constexpr int kWarps = kThreads / 32;
+constexpr int kBins0 = 2048;              // first digit: key bits 31..21
+constexpr int kBins = 256;                // candidate digits: 8 bits
+constexpr int kHists = 4;                 // warp w adds into first-digit histogram w % kHists
+constexpr int kChunk = 36 * 1024;         // keys held in shared memory at a time
+constexpr int kCand = 4096;               // candidates (keys in the threshold bin) kept
+constexpr int kMaxTopk = 16384;
+constexpr unsigned kStatusTimeout = 1u;
+
+__device__ unsigned int g_topk_status = 0;
+
+struct Params {
+  const float* logits;
+  long long stride0;                // elements between rows
+  long long num_rows;
+  const int32_t* seq_lens;          // decode (with next_n), or nullptr
+  int next_n;
+  const int32_t* row_starts;        // prefill, or nullptr
+  const int32_t* row_ends;
+  int32_t* out;
+  long long out_stride;
+  int k;
+  unsigned long long timeout_ns;
+};
+
+// shared memory (32-bit words): keys (+4 alignment pad), kHists first-digit
+// histograms, the merged histogram, candidate keys and positions, per-warp
+// counts, control words, one mbarrier
+constexpr size_t kSmemWords = kChunk + 4 + kHists * kBins0 + kBins0 + 2 * kCand + 4 * kWarps + 16;
+constexpr size_t kSmemBytes = sizeof(uint32_t) * kSmemWords + 16;
+
+__device__ __forceinline__ uint32_t order_key(const float x) {
+  const uint32_t b = __float_as_uint(x);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+__device__ __forceinline__ uint64_t now_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Block-wide search over `nb` bins (a multiple of kThreads, or kBins with
+// threads >= kBins idle): finds the digit d with count(> d) < need <=
+// count(>= d) and leaves d, count(> d) and count(d) in ctl[0..2].
+__device__ __forceinline__ void find_digit(const uint32_t* hist, int nb, uint32_t need,
+                                           uint32_t* wsum, uint32_t* ctl) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int bpt = nb >= kThreads ? nb / kThreads : 1;
+  const bool owns = tid * bpt < nb;
+  uint32_t s = 0;
+  if (owns)
+    for (int j = 0; j < bpt; ++j) s += hist[bpt * tid + j];
+  uint32_t incl = s;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const uint32_t v = __shfl_down_sync(0xFFFFFFFFu, incl, off);
+    if (lane + off < 32) incl += v;
+  }
+  if (lane == 0) wsum[warp] = incl;
+  __syncthreads();
+  for (int w = warp + 1; w < kWarps; ++w) incl += wsum[w];
+  uint32_t above = incl - s;
+  if (owns && above < need && need <= incl) {
+    for (int j = bpt - 1; j >= 0; --j) {
+      const uint32_t c = hist[bpt * tid + j];
+      if (above + c >= need) {
+        ctl[0] = static_cast<uint32_t>(bpt * tid + j);
+        ctl[1] = above;
+        ctl[2] = c;
+        break;
+      }
+      above += c;
+    }
+  }
+  __syncthreads();
+}
+
+// Block-wide exclusive prefix sums of two per-thread counts (thread order):
+// returns this thread's offsets and the block totals. Uses scratch[2 * kWarps].
+__device__ __forceinline__ void block_scan2(uint32_t a, uint32_t b, uint32_t* scratch,
+                                            uint32_t& ea, uint32_t& eb, uint32_t& ta,
+                                            uint32_t& tb) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t sa = a, sb = b;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const uint32_t xa = __shfl_up_sync(0xFFFFFFFFu, sa, off);
+    const uint32_t xb = __shfl_up_sync(0xFFFFFFFFu, sb, off);
+    if (lane >= off) {
+      sa += xa;
+      sb += xb;
+    }
+  }
+  if (lane == 31) {
+    scratch[warp] = sa;
+    scratch[kWarps + warp] = sb;
+  }
+  __syncthreads();
+  uint32_t pa = 0, pb = 0;
+  ta = tb = 0;
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) {
+    const uint32_t wa = scratch[w], wb = scratch[kWarps + w];
+    if (w < warp) {
+      pa += wa;
+      pb += wb;
+    }
+    ta += wa;
+    tb += wb;
+  }
+  ea = pa + sa - a;
+  eb = pb + sb - b;
+  __syncthreads();   // scratch may be reused right after
+}
+
+__global__ void __launch_bounds__(kThreads, 1) topk_per_row_kernel(const Params p) {
+  extern __shared__ __align__(16) uint32_t smem[];
+  uint32_t* const keys_raw = smem;                               // [kChunk + 4]
+  uint32_t* const whist = smem + kChunk + 4;                     // [kHists][kBins0]
+  uint32_t* const hist = whist + kHists * kBins0;                // [kBins0]
+  uint32_t* const cand_key = hist + kBins0;                      // [kCand]
+  uint32_t* const cand_pos = cand_key + kCand;                   // [kCand]
+  uint32_t* const wcnt = cand_pos + kCand;                       // [4][kWarps]
+  uint32_t* const wsum = wcnt + 2 * kWarps;                      // [kWarps] (scan scratch)
+  uint32_t* const ctl = wcnt + 4 * kWarps;                       // [8]
+  const uint32_t bar = static_cast<uint32_t>(__cvta_generic_to_shared(ctl + 8));
+
+  const long long row = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  long long start, end;
+  if (p.seq_lens != nullptr) {
+    start = 0;
+    end = static_cast<long long>(p.seq_lens[row / p.next_n]) - p.next_n + row % p.next_n + 1;
+  } else {
+    start = p.row_starts[row];
+    end = p.row_ends[row];
+  }
+  const long long len = end > start ? end - start : 0;
+  int32_t* const out = p.out + row * p.out_stride;
+  const int k = p.k;
+  if (len <= k) {
+    for (int i = tid; i < k; i += kThreads) out[i] = i < len ? i : -1;
+    return;
+  }
+  const float* const src = p.logits + row * p.stride0 + start;
+  const bool one_chunk = len <= kChunk;
+
+  // The row goes through shared memory in chunks of kChunk values (a row
+  // that fits is loaded once): each chunk's 16-byte aligned interior by one
+  // bulk copy, its ragged ends (< 4 values each) by plain loads. kChunk is a
+  // multiple of 4, so every chunk starts at the same offset within 16 bytes,
+  // and `pad` puts its interior on a 16-byte boundary: keys[i] holds value
+  // c0 + i, converted to its key in place.
+  const uint32_t head = static_cast<uint32_t>(((16u - (reinterpret_cast<uintptr_t>(src) & 15u)) & 15u) >> 2);
+  uint32_t* const keys = keys_raw + ((4u - head) & 3u);
+  if (tid == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  uint32_t phase = 0;
+  auto load_chunk = [&](long long c0, long long clen) {
+    const long long h = head < clen ? head : clen;
+    const long long body = ((clen - h) / 4) * 4;
+    if (tid == 0) {
+      const uint32_t bytes = static_cast<uint32_t>(body * 4);
+      asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
+                   "r"(bytes)
+                   : "memory");
+      if (bytes > 0)
+        asm volatile(
+            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                static_cast<uint32_t>(__cvta_generic_to_shared(keys + h))),
+            "l"(src + c0 + h), "r"(bytes), "r"(bar)
+            : "memory");
+    }
+    if (tid < h) keys[tid] = __float_as_uint(src[c0 + tid]);
+    const long long tail0 = h + body;
+    if (tid < clen - tail0) keys[tail0 + tid] = __float_as_uint(src[c0 + tail0 + tid]);
+    uint32_t done = 0;
+    const uint64_t t0 = now_ns();
+    while (true) {
+      asm volatile(
+          "{\n\t.reg .pred q;\n\tmbarrier.try_wait.parity.acquire.cta.shared::cta.b64 q, [%1], %2;\n\t"
+          "selp.u32 %0, 1, 0, q;\n\t}"
+          : "=r"(done)
+          : "r"(bar), "r"(phase)
+          : "memory");
+      if (done) break;
+      if (now_ns() - t0 > p.timeout_ns) {
+        if (tid == 0) atomicOr(&g_topk_status, kStatusTimeout);
+        break;
+      }
+    }
+    phase ^= 1u;
+    __syncthreads();
+  };
+
+  // ---- first digit (11 bits) over the whole row; keys are formed in place
+  uint32_t* const my_hist = whist + (warp % kHists) * kBins0;
+  for (int i = tid; i < kHists * kBins0; i += kThreads) whist[i] = 0;
+  __syncthreads();
+#pragma unroll 1
+  for (long long c0 = 0; c0 < len; c0 += kChunk) {
+    const long long clen = len - c0 < kChunk ? len - c0 : kChunk;
+    load_chunk(c0, clen);
+#pragma unroll 4
+    for (long long i = tid; i < clen; i += kThreads) {
+      const uint32_t u = order_key(__uint_as_float(keys[i]));
+      keys[i] = u;
+      atomicAdd(&my_hist[u >> 21], 1u);
+    }
+    __syncthreads();
+  }
+  for (int b = tid; b < kBins0; b += kThreads) {
+    uint32_t c = 0;
+#pragma unroll
+    for (int w = 0; w < kHists; ++w) c += whist[w * kBins0 + b];
+    hist[b] = c;
+  }
+  __syncthreads();
+  find_digit(hist, kBins0, static_cast<uint32_t>(k), wsum, ctl);
+  const uint32_t d0 = ctl[0];
+  uint32_t k_rem = static_cast<uint32_t>(k) - ctl[1];
+  const uint32_t c0_count = ctl[2];
+  const uint32_t n_gt0 = ctl[1];
+  __syncthreads();
+
+  // ---- one pass over the row: positions with a first digit above d0 go out
+  // (slots [0, n_gt0)); those equal to d0 are the candidates. Thread t takes
+  // positions t, t + kThreads, ... of each chunk (conflict-free shared reads),
+  // counts its two classes, and a block scan of the counts gives it the
+  // slots it writes, in order; no atomics. The output order is thread-major,
+  // which the contract leaves open.
+  const bool keep = c0_count <= static_cast<uint32_t>(kCand);
+  uint32_t gt_base = 0, eq_base = 0;
+#pragma unroll 1
+  for (long long c0 = 0; c0 < len; c0 += kChunk) {
+    const long long clen = len - c0 < kChunk ? len - c0 : kChunk;
+    if (!one_chunk) {
+      load_chunk(c0, clen);
+      for (long long i = tid; i < clen; i += kThreads) keys[i] = order_key(__uint_as_float(keys[i]));
+      __syncthreads();
+    }
+    const int n_mine = static_cast<int>((clen - tid + kThreads - 1) / kThreads);
+    uint32_t ng = 0, ne = 0;
+#pragma unroll 4
+    for (int j = 0; j < n_mine; ++j) {
+      const uint32_t dg = keys[tid + j * kThreads] >> 21;
+      ng += dg > d0;
+      ne += dg == d0;
+    }
+    uint32_t og, oe, tg, te;
+    block_scan2(ng, ne, wcnt, og, oe, tg, te);
+    og += gt_base;
+    oe += eq_base;
+    for (int j = 0; j < n_mine; ++j) {
+      const long long i = tid + static_cast<long long>(j) * kThreads;
+      const uint32_t u = keys[i];
+      const uint32_t dg = u >> 21;
+      if (dg > d0) {
+        out[og++] = static_cast<int32_t>(c0 + i);
+      } else if (dg == d0) {
+        if (keep) {
+          cand_key[oe] = u;
+          cand_pos[oe] = static_cast<uint32_t>(c0 + i);
+        } else if (c0_count == k_rem) {
+          out[n_gt0 + oe] = static_cast<int32_t>(c0 + i);   // the whole bin is taken
+        }
+        ++oe;
+      }
+    }
+    gt_base += tg;
+    eq_base += te;
+    __syncthreads();
+  }
+  if (c0_count == k_rem && !keep) return;   // the whole threshold bin went out above
+
+  // ---- the k_rem largest of the threshold bin's keys (bits 20..0 still open)
+  int32_t* const out_c = out + n_gt0;
+  if (keep) {
+    // candidates in shared memory: 8-bit digits over bits 20..0 (13/8 split:
+    // a 5-bit digit first, then two 8-bit digits)
+    uint32_t prefix = d0 << 21, mask = 0xFFE00000u;
+    const int shifts[3] = {16, 8, 0};
+    const uint32_t widths[3] = {0x1Fu, 0xFFu, 0xFFu};
+    bool settled = c0_count == k_rem;
+    const int n = static_cast<int>(c0_count);
+#pragma unroll 1
+    for (int pss = 0; pss < 3 && !settled; ++pss) {
+      for (int i = tid; i < kBins; i += kThreads) hist[i] = 0;
+      __syncthreads();
+      for (int i = tid; i < n; i += kThreads) {
+        const uint32_t u = cand_key[i];
+        if ((u & mask) == prefix) atomicAdd(&hist[(u >> shifts[pss]) & widths[pss]], 1u);
+      }
+      __syncthreads();
+      find_digit(hist, kBins, k_rem, wsum, ctl);
+      prefix |= ctl[0] << shifts[pss];
+      mask |= widths[pss] << shifts[pss];
+      k_rem -= ctl[1];
+      settled = ctl[2] == k_rem;
+      __syncthreads();
+    }
+    // candidates above the prefix, then the first k_rem equal to it: per-thread
+    // counts over a strided share of the candidates and a block scan
+    const uint32_t n_above = static_cast<uint32_t>(k) - n_gt0 - k_rem;
+    uint32_t ng = 0, ne = 0;
+    for (int i = tid; i < n; i += kThreads) {
+      const uint32_t u = cand_key[i] & mask;
+      ng += u > prefix;
+      ne += u == prefix;
+    }
+    uint32_t og, oe, tg, te;
+    block_scan2(ng, ne, wcnt, og, oe, tg, te);
+    for (int i = tid; i < n; i += kThreads) {
+      const uint32_t u = cand_key[i] & mask;
+      if (u > prefix) {
+        out_c[og++] = static_cast<int32_t>(cand_pos[i]);
+      } else if (u == prefix) {
+        if (oe < k_rem) out_c[n_above + oe] = static_cast<int32_t>(cand_pos[i]);
+        ++oe;
+      }
+    }
+    return;
+  }
+
+  // ---- too many candidates to keep: 8-bit digit passes over the whole row
+  // for bits 20..0, then one output pass for the bin (rare: a row where more
+  // than kCand values share the top 11 key bits with the k-th largest)
+  uint32_t prefix = d0 << 21, mask = 0xFFE00000u;
+  const int shifts[3] = {13, 5, 0};
+  const uint32_t widths[3] = {0xFFu, 0xFFu, 0x1Fu};
+  bool settled = false;
+#pragma unroll 1
+  for (int pss = 0; pss < 3 && !settled; ++pss) {
+    for (int i = tid; i < kBins; i += kThreads) hist[i] = 0;
+    __syncthreads();
+#pragma unroll 1
+    for (long long c0 = 0; c0 < len; c0 += kChunk) {
+      const long long clen = len - c0 < kChunk ? len - c0 : kChunk;
+      if (!one_chunk) {
+        load_chunk(c0, clen);
+        for (long long i = tid; i < clen; i += kThreads) keys[i] = order_key(__uint_as_float(keys[i]));
+        __syncthreads();
+      }
+      for (long long i = tid; i < clen; i += kThreads) {
+        const uint32_t u = keys[i];
+        if ((u & mask) == prefix) atomicAdd(&hist[(u >> shifts[pss]) & widths[pss]], 1u);
+      }
+      __syncthreads();
+    }
+    find_digit(hist, kBins, k_rem, wsum, ctl);
+    prefix |= ctl[0] << shifts[pss];
+    mask |= widths[pss] << shifts[pss];
+    k_rem -= ctl[1];
+    settled = ctl[2] == k_rem;
+    __syncthreads();
+  }
+  const uint32_t n_above = static_cast<uint32_t>(k) - n_gt0 - k_rem;
+  uint32_t g_base = 0, e_base = 0;
+#pragma unroll 1
+  for (long long c0 = 0; c0 < len; c0 += kChunk) {
+    const long long clen = len - c0 < kChunk ? len - c0 : kChunk;
+    if (!one_chunk) {
+      load_chunk(c0, clen);
+      for (long long i = tid; i < clen; i += kThreads) keys[i] = order_key(__uint_as_float(keys[i]));
+      __syncthreads();
+    }
+    uint32_t ng = 0, ne = 0;
+    for (long long i = tid; i < clen; i += kThreads) {
+      const uint32_t u = keys[i];
+      const bool in_bin = (u & 0xFFE00000u) == (d0 << 21);
+      ng += in_bin && (u & mask) > prefix;
+      ne += in_bin && (u & mask) == prefix;
+    }
+    uint32_t og, oe, tg, te;
+    block_scan2(ng, ne, wcnt, og, oe, tg, te);
+    og += g_base;
+    oe += e_base;
+    for (long long i = tid; i < clen; i += kThreads) {
+      const uint32_t u = keys[i];
+      if ((u & 0xFFE00000u) != (d0 << 21)) continue;
+      if ((u & mask) > prefix) {
+        out_c[og++] = static_cast<int32_t>(c0 + i);
+      } else if ((u & mask) == prefix) {
+        if (oe < k_rem) out_c[n_above + oe] = static_cast<int32_t>(c0 + i);
+        ++oe;
+      }
+    }
+    g_base += tg;
+    e_base += te;
+    __syncthreads();
+  }
+}
+
+bool g_attr_set[64] = {};
+
+}  // namespace topk
+}  // namespace glm53
+
+using namespace glm53::topk;
+
+extern "C" int glm53_topk_per_row(const float* logits, int64_t num_rows, int64_t stride0,
+                                  int64_t stride1, const int32_t* seq_lens, int next_n,
+                                  const int32_t* row_starts, const int32_t* row_ends,
+                                  int32_t* out, int64_t out_stride, int topk, void* stream) {
+  if (num_rows < 0 || stride0 < 0 || out_stride < topk) return GLM53_ERR_RANK;
+  if (topk <= 0 || topk > kMaxTopk) return GLM53_ERR_TOPK;
+  if (stride1 != 1) return GLM53_ERR_RANK;           // rows must be contiguous
+  const bool decode = seq_lens != nullptr;
+  if (decode == (row_starts != nullptr || row_ends != nullptr)) return GLM53_ERR_RANK;
+  if (!decode && (row_starts == nullptr || row_ends == nullptr)) return GLM53_ERR_RANK;
+  if (decode && next_n <= 0) return GLM53_ERR_RANK;
+  if (num_rows == 0) return GLM53_OK;
+  if (logits == nullptr || out == nullptr) return GLM53_ERR_ALIGN;
+  if ((reinterpret_cast<uintptr_t>(logits) & 3u) || (reinterpret_cast<uintptr_t>(out) & 3u))
+    return GLM53_ERR_ALIGN;
+  if (num_rows > 0x7FFFFFFFll) return GLM53_ERR_RANK;
+  int dev = 0, major = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+    return GLM53_ERR_CUDA;
+  if (major != 10) return GLM53_ERR_DEVICE;
+  if (dev < 0 || dev >= 64) return GLM53_ERR_DEVICE;
+  // Opt in to the large dynamic shared-memory size once per device, before
+  // any capture (the host call itself is not capturable).
+  if (!g_attr_set[dev]) {
+    if (cudaFuncSetAttribute(topk_per_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kSmemBytes)) != cudaSuccess)
+      return GLM53_ERR_CUDA;
+    g_attr_set[dev] = true;
+  }
+  Params p;
+  p.logits = logits;
+  p.stride0 = stride0;
+  p.num_rows = num_rows;
+  p.seq_lens = seq_lens;
+  p.next_n = next_n;
+  p.row_starts = row_starts;
+  p.row_ends = row_ends;
+  p.out = out;
+  p.out_stride = out_stride;
+  p.k = topk;
+  p.timeout_ns = 1000000000ull;
+  topk_per_row_kernel<<<static_cast<unsigned>(num_rows), kThreads, kSmemBytes,
+                        static_cast<cudaStream_t>(stream)>>>(p);
+  return cudaGetLastError() == cudaSuccess ? GLM53_OK : GLM53_ERR_CUDA;
+}
+
+extern "C" int glm53_topk_status(uint32_t* status, int clear) {
+  unsigned int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_topk_status, sizeof(v)) != cudaSuccess) return GLM53_ERR_CUDA;
+  if (status) *status = v;
+  if (clear) {
+    const unsigned int zero = 0;
+    if (cudaMemcpyToSymbol(g_topk_status, &zero, sizeof(zero)) != cudaSuccess) return GLM53_ERR_CUDA;
+  }
+  return GLM53_OK;
+}

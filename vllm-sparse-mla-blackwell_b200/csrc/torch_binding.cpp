@@ -10,7 +10,9 @@
 // through glm53_sparse_mla_fwd_ws on the caller's current CUDA stream.
 // `sparse_fwd_paged` takes vLLM's request-local positions directly, and
 // `concat_and_cache_mla` is the latent KV-cache write that feeds the op, with
-// the schema of vLLM's cache op of that name.
+// the schema of vLLM's cache op of that name; `top_k_per_row_decode` /
+// `top_k_per_row_prefill` produce the top-k positions from the indexer's
+// logits with the schemas of vLLM's ops of those names.
 
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
@@ -207,11 +209,69 @@ void concat_and_cache_mla(const torch::Tensor& kv_c, const torch::Tensor& k_pe,
   TORCH_CHECK(rc == GLM53_OK, "glm53_sparse_mla: ", glm53_sparse_mla_strerror(rc));
 }
 
+// Indexer top-k with the schemas of vLLM's top_k_per_row_decode /
+// top_k_per_row_prefill (vllm 0.22.0 vllm/_custom_ops.py:2799-2840). seq_lens
+// may be 1-D [B] (row r ends at seq_lens[r / next_n] - next_n + r % next_n + 1)
+// or 2-D [B, next_n] (row r ends at the r-th entry: per-token context lengths).
+void run_topk(const torch::Tensor& logits, const int32_t* seq_lens, int64_t next_n,
+              const int32_t* starts, const int32_t* ends, torch::Tensor& out, int64_t num_rows,
+              int64_t stride0, int64_t stride1, int64_t topk) {
+  TORCH_CHECK(logits.is_cuda() && out.is_cuda(), "glm53_sparse_mla: logits and indices must be CUDA tensors");
+  TORCH_CHECK(logits.scalar_type() == torch::kFloat, "glm53_sparse_mla: logits must be float32");
+  TORCH_CHECK(out.scalar_type() == torch::kInt && out.dim() == 2 && out.stride(1) == 1,
+              "glm53_sparse_mla: raw_topk_indices must be int32 [rows, >= topk] with contiguous rows");
+  TORCH_CHECK(num_rows <= out.size(0) && topk <= out.size(1),
+              "glm53_sparse_mla: raw_topk_indices is smaller than [num_rows, topk_tokens]");
+  TORCH_CHECK(num_rows <= 0 || (num_rows - 1) * stride0 < logits.numel(),
+              "glm53_sparse_mla: num_rows * stride0 exceeds logits");
+  if (num_rows == 0) return;
+  const c10::cuda::CUDAGuard guard(logits.device());
+  cudaStream_t stream = c10::cuda::getCurrentCUDAStream(logits.get_device()).stream();
+  const int rc = glm53_topk_per_row(logits.data_ptr<float>(), num_rows, stride0, stride1, seq_lens,
+                                    static_cast<int>(next_n), starts, ends, out.data_ptr<int32_t>(),
+                                    out.stride(0), static_cast<int>(topk), static_cast<void*>(stream));
+  TORCH_CHECK(rc == GLM53_OK, "glm53_sparse_mla: ", glm53_sparse_mla_strerror(rc));
+}
+
+void top_k_per_row_decode(const torch::Tensor& logits, int64_t next_n, const torch::Tensor& seq_lens,
+                          torch::Tensor& raw_topk_indices, int64_t num_rows, int64_t stride0,
+                          int64_t stride1, int64_t topk_tokens) {
+  TORCH_CHECK(seq_lens.is_cuda() && seq_lens.scalar_type() == torch::kInt && seq_lens.is_contiguous(),
+              "glm53_sparse_mla: seq_lens must be a contiguous int32 CUDA tensor");
+  TORCH_CHECK(next_n >= 1, "glm53_sparse_mla: next_n must be >= 1");
+  int64_t nn = next_n;
+  if (seq_lens.dim() == 2 && seq_lens.size(1) > 1) {
+    TORCH_CHECK(seq_lens.size(1) == next_n && seq_lens.numel() >= num_rows,
+                "glm53_sparse_mla: 2-D seq_lens must be [B, next_n] covering num_rows");
+    nn = 1;   // per-row context lengths
+  } else {
+    TORCH_CHECK(seq_lens.dim() >= 1 && seq_lens.numel() * next_n >= num_rows,
+                "glm53_sparse_mla: seq_lens must hold ceil(num_rows / next_n) lengths");
+  }
+  run_topk(logits, seq_lens.data_ptr<int32_t>(), nn, nullptr, nullptr, raw_topk_indices, num_rows,
+           stride0, stride1, topk_tokens);
+}
+
+void top_k_per_row_prefill(const torch::Tensor& logits, const torch::Tensor& cu_seqlen_ks,
+                           const torch::Tensor& cu_seqlen_ke, torch::Tensor& raw_topk_indices,
+                           int64_t num_rows, int64_t stride0, int64_t stride1, int64_t topk_tokens) {
+  TORCH_CHECK(cu_seqlen_ks.is_cuda() && cu_seqlen_ke.is_cuda() &&
+                  cu_seqlen_ks.scalar_type() == torch::kInt && cu_seqlen_ke.scalar_type() == torch::kInt &&
+                  cu_seqlen_ks.is_contiguous() && cu_seqlen_ke.is_contiguous() &&
+                  cu_seqlen_ks.numel() >= num_rows && cu_seqlen_ke.numel() >= num_rows,
+              "glm53_sparse_mla: cu_seqlen_ks / cu_seqlen_ke must be contiguous int32 CUDA tensors "
+              "with num_rows entries");
+  run_topk(logits, nullptr, 1, cu_seqlen_ks.data_ptr<int32_t>(), cu_seqlen_ke.data_ptr<int32_t>(),
+           raw_topk_indices, num_rows, stride0, stride1, topk_tokens);
+}
+
 TORCH_LIBRARY(glm53_sparse_mla, m) {
   m.def("sparse_fwd(Tensor q, Tensor kv, Tensor indices, float sm_scale, float kv_scale, Tensor(a!) out) -> ()");
   m.def("sparse_fwd_lse(Tensor q, Tensor kv, Tensor indices, float sm_scale, float kv_scale, Tensor(a!) out, Tensor(b!) lse) -> ()");
   m.def("sparse_fwd_paged(Tensor q, Tensor kv, Tensor topk_positions, Tensor req_id_per_token, Tensor block_table, int block_size, int topk, float sm_scale, float kv_scale, Tensor(a!) out, Tensor(b!)? lse=None, int block_stride_rows=0) -> ()");
   m.def("concat_and_cache_mla(Tensor kv_c, Tensor k_pe, Tensor(a!) kv_cache, Tensor slot_mapping, str kv_cache_dtype, Tensor scale) -> ()");
+  m.def("top_k_per_row_decode(Tensor logits, int next_n, Tensor seq_lens, Tensor(a!) raw_topk_indices, int num_rows, int stride0, int stride1, int topk_tokens) -> ()");
+  m.def("top_k_per_row_prefill(Tensor logits, Tensor cu_seqlen_ks, Tensor cu_seqlen_ke, Tensor(a!) raw_topk_indices, int num_rows, int stride0, int stride1, int topk_tokens) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(glm53_sparse_mla, CUDA, m) {
@@ -219,4 +279,6 @@ TORCH_LIBRARY_IMPL(glm53_sparse_mla, CUDA, m) {
   m.impl("sparse_fwd_lse", &sparse_fwd_lse);
   m.impl("sparse_fwd_paged", &sparse_fwd_paged);
   m.impl("concat_and_cache_mla", &concat_and_cache_mla);
+  m.impl("top_k_per_row_decode", &top_k_per_row_decode);
+  m.impl("top_k_per_row_prefill", &top_k_per_row_prefill);
 }

@@ -24,6 +24,8 @@ __all__ = [
     "sparse_fwd_with_lse",
     "sparse_fwd_paged",
     "concat_and_cache_mla",
+    "top_k_per_row_decode",
+    "top_k_per_row_prefill",
     "HEADS_PER_RANK",
     "SUPPORTED_HEADS_PER_RANK",
     "KV_LORA_RANK",
@@ -153,6 +155,35 @@ def concat_and_cache_mla(kv_c, k_pe, kv_cache, slot_mapping, kv_cache_dtype, sca
                                                     str(kv_cache_dtype), scale)
 
 
+def top_k_per_row_decode(logits, next_n, seq_lens, raw_topk_indices, num_rows, stride0, stride1,
+                         topk_tokens):
+    """Top-k positions of each decode row of the indexer's logits.
+
+    Row r covers ``logits[r, :end)`` with ``end = seq_lens[r // next_n] -
+    next_n + r % next_n + 1`` (1-D seq_lens) or ``seq_lens.flatten()[r]``
+    (2-D [B, next_n]); ``raw_topk_indices[r, :topk_tokens]`` receives
+    0..end-1 then -1 when end <= topk_tokens, else the positions of the
+    topk_tokens largest logits in no particular order. Same arguments as
+    vLLM's ``ops.top_k_per_row_decode`` (vllm 0.22.0
+    vllm/_custom_ops.py:2821-2840).
+    """
+    torch.ops.glm53_sparse_mla.top_k_per_row_decode(
+        logits, int(next_n), seq_lens, raw_topk_indices, int(num_rows), int(stride0),
+        int(stride1), int(topk_tokens))
+
+
+def top_k_per_row_prefill(logits, cu_seqlen_ks, cu_seqlen_ke, raw_topk_indices, num_rows,
+                          stride0, stride1, topk_tokens):
+    """Top-k positions of each prefill row: row r covers
+    ``logits[r, cu_seqlen_ks[r]:cu_seqlen_ke[r])`` and its positions are
+    written relative to cu_seqlen_ks[r]. Same arguments as vLLM's
+    ``ops.top_k_per_row_prefill`` (vllm 0.22.0 vllm/_custom_ops.py:2799-2818).
+    """
+    torch.ops.glm53_sparse_mla.top_k_per_row_prefill(
+        logits, cu_seqlen_ks, cu_seqlen_ke, raw_topk_indices, int(num_rows), int(stride0),
+        int(stride1), int(topk_tokens))
+
+
 # Shape-only meta kernels so torch.compile can trace through the ops.
 @torch.library.register_fake("glm53_sparse_mla::sparse_fwd")
 def _sparse_fwd_fake(q, kv, indices, sm_scale, kv_scale, out):
@@ -180,4 +211,18 @@ def _sparse_fwd_paged_fake(q, kv, topk_positions, req_id_per_token, block_table,
 @torch.library.register_fake("glm53_sparse_mla::concat_and_cache_mla")
 def _concat_and_cache_mla_fake(kv_c, k_pe, kv_cache, slot_mapping, kv_cache_dtype, scale):
     torch._check(kv_c.dim() == 2 and kv_cache.dim() == 3 and slot_mapping.dim() == 1)
+    return None
+
+
+@torch.library.register_fake("glm53_sparse_mla::top_k_per_row_decode")
+def _top_k_per_row_decode_fake(logits, next_n, seq_lens, raw_topk_indices, num_rows, stride0,
+                               stride1, topk_tokens):
+    torch._check(raw_topk_indices.dim() == 2)
+    return None
+
+
+@torch.library.register_fake("glm53_sparse_mla::top_k_per_row_prefill")
+def _top_k_per_row_prefill_fake(logits, cu_seqlen_ks, cu_seqlen_ke, raw_topk_indices, num_rows,
+                                stride0, stride1, topk_tokens):
+    torch._check(raw_topk_indices.dim() == 2)
     return None
