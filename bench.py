@@ -40,6 +40,9 @@ oracle port) on the host cores instead, on rank 0 only.
 feeds the attention): --tokens new tokens per step (default 8192, a
 chunked-prefill step) into a 524288-slot paged cache, --kv fp8 (default bf16)
 for the plain fp8 cache, same JSON line with its own metric and roofline.
+--op topk measures the indexer's per-row top-2048 over --rows decode rows of
+--ctx logits (default 32 x 8192, C2's batch and context), with vLLM's
+compiled op of the same contract timed alongside when it loads.
 """
 
 from __future__ import annotations
@@ -71,10 +74,13 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--op", choices=["attention", "cache_write"], default="attention",
-                    help="attention (the headline) or the latent KV-cache writer")
+    ap.add_argument("--op", choices=["attention", "cache_write", "topk"], default="attention",
+                    help="attention (the headline), the latent KV-cache writer, or the "
+                         "indexer's per-row top-k")
     ap.add_argument("--tokens", type=int, default=8192,
                     help="cache_write: new tokens per step (a chunked-prefill step)")
+    ap.add_argument("--rows", type=int, default=32, help="topk: decode rows (query tokens)")
+    ap.add_argument("--ctx", type=int, default=8192, help="topk: context length per row")
     ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5"], default="c2")
     ap.add_argument("--heads", type=int, default=0, help="heads per launch (0 = workload's)")
     ap.add_argument("--kv", choices=["bf16", "fp8"], default="bf16", help="C5 KV dtype")
@@ -403,24 +409,10 @@ def cache_write_desc(args, fp8: bool) -> dict:
             "tokens_per_step": args.tokens, "kv_dtype": "fp8_e4m3" if fp8 else "bf16"}
 
 
-def run_cache_write(args, dist: Dist):
-    torch.cuda.set_device(dist.local)
-    device = torch.device("cuda", dist.local)
-    dist.init("nccl")
-    import glm53_sparse_mla as G
-    fp8 = args.kv == "fp8"
-    dtype = "fp8" if fp8 else "auto"
-    cache = torch.zeros((CACHE_POOL_SLOTS // CACHE_BLOCK, CACHE_BLOCK, 512),
-                        dtype=torch.uint8 if fp8 else torch.bfloat16, device=device)
-    scale = torch.tensor([0.05 if fp8 else 1.0], dtype=torch.float32, device=device)
-    sets = cache_write_sets(args, device, max(1, args.sets), 300 + 1000 * dist.rank)
-    empty_pe = sets[0][0][:, :0]
-
-    def step(k):
-        kv_c, slots = sets[k % len(sets)]
-        G.concat_and_cache_mla(kv_c, empty_pe, cache, slots, dtype, scale)
-
-    stream = torch.cuda.Stream(device)
+def time_graph(step, args, dist: Dist, device, stream):
+    """Warm-up, then K steps captured in one CUDA graph, timed with CUDA
+    events on `stream` between barriers, clocks sampled during the run.
+    Returns (ms per step on this rank, ms per step max over ranks, clocks)."""
     with torch.cuda.stream(stream):
         for k in range(max(args.warmup, 3)):
             step(k)
@@ -446,12 +438,35 @@ def run_cache_write(args, dist: Dist):
             e1.record(stream)
         torch.cuda.synchronize()
         dist.barrier()
-    ms_local = e0.elapsed_time(e1)
-    ms_step = dist.max(ms_local, device) / args.steps
+    ms_local = e0.elapsed_time(e1) / args.steps
+    del graph
+    torch.cuda.synchronize()
+    return ms_local, dist.max(ms_local * args.steps, device) / args.steps, clk.summary()
+
+
+def run_cache_write(args, dist: Dist):
+    torch.cuda.set_device(dist.local)
+    device = torch.device("cuda", dist.local)
+    dist.init("nccl")
+    import glm53_sparse_mla as G
+    fp8 = args.kv == "fp8"
+    dtype = "fp8" if fp8 else "auto"
+    cache = torch.zeros((CACHE_POOL_SLOTS // CACHE_BLOCK, CACHE_BLOCK, 512),
+                        dtype=torch.uint8 if fp8 else torch.bfloat16, device=device)
+    scale = torch.tensor([0.05 if fp8 else 1.0], dtype=torch.float32, device=device)
+    sets = cache_write_sets(args, device, max(1, args.sets), 300 + 1000 * dist.rank)
+    empty_pe = sets[0][0][:, :0]
+
+    def step(k):
+        kv_c, slots = sets[k % len(sets)]
+        G.concat_and_cache_mla(kv_c, empty_pe, cache, slots, dtype, scale)
+
+    stream = torch.cuda.Stream(device)
+    ms_rank, ms_step, clocks = time_graph(step, args, dist, device, stream)
     value = args.tokens * dist.world / (ms_step / 1e3)
     alg = cache_write_bytes(args.tokens, fp8)
     hbm_peak, _, peak_kind = measured_peaks()
-    achieved = alg / (ms_local / args.steps / 1e3) / 1e9
+    achieved = alg / (ms_rank / 1e3) / 1e9
     m = None
     prof = os.path.join(REPO, "profiles", f"kv_cache_writer_{args.kv}.md")
     if os.path.exists(prof):
@@ -459,8 +474,6 @@ def run_cache_write(args, dist: Dist):
     roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
             "frac": round(achieved / hbm_peak, 4), "peak_source": peak_kind,
             "traffic": int(m.group(1)) if m else None, "algorithmic_bytes_per_launch": alg}
-    del graph
-    torch.cuda.synchronize()
     e2e = None
     if not args.no_e2e:
         # host buffers: each step copies kv_c and slots in, writes, and reads
@@ -513,7 +526,7 @@ def run_cache_write(args, dist: Dist):
                 "data": "synthetic (seeded)", "config": cfg, "roofline": roof,
                 "cpu_baseline": cpu, "e2e": e2e,
                 "gpu_launches": args.steps + (args.steps if e2e else 0),
-                "clocks": clk.summary()}
+                "clocks": clocks}
         print(json.dumps(line), flush=True)
     dist.close()
 
@@ -538,6 +551,149 @@ def cache_write_cpu(one_set, fp8: bool, seconds: float):
     return {"value": round(done / dt, 2), "unit": CW_UNIT, "cores": 1, "kind": "port",
             "sample": f"{done} tokens in batches of {n}, numpy oracle (restates vLLM's "
                       f"concat_and_cache_mla), {dt:.1f} s"}
+
+
+# ---------------------------------------------------------------------------
+# the indexer's per-row top-k (--op topk)
+# ---------------------------------------------------------------------------
+TOPK_K = 2048
+TK_UNIT = "rows/s"
+
+
+def topk_sets(args, device, n_sets: int, seed0: int = 500):
+    g = torch.Generator(device="cpu")
+    out = []
+    for s in range(n_sets):
+        g.manual_seed(seed0 + s)
+        out.append(torch.randn((args.rows, args.ctx), generator=g).to(device))
+    return out
+
+
+def topk_desc(args) -> dict:
+    return {"workload": f"indexer top-{TOPK_K} per decode row: {args.rows} rows x {args.ctx} "
+                        "fp32 logits (the context), seeded N(0, 1)",
+            "rows_per_step": args.rows, "ctx": args.ctx, "topk": TOPK_K}
+
+
+def run_topk(args, dist: Dist):
+    torch.cuda.set_device(dist.local)
+    device = torch.device("cuda", dist.local)
+    dist.init("nccl")
+    import glm53_sparse_mla as G
+    sets = topk_sets(args, device, max(1, args.sets), 500 + 1000 * dist.rank)
+    seq = torch.full((args.rows,), args.ctx, dtype=torch.int32, device=device)
+    out = torch.empty((args.rows, TOPK_K), dtype=torch.int32, device=device)
+
+    def step(k):
+        G.top_k_per_row_decode(sets[k % len(sets)], 1, seq, out, args.rows, args.ctx, 1, TOPK_K)
+
+    stream = torch.cuda.Stream(device)
+    ms_rank, ms_step, clocks = time_graph(step, args, dist, device, stream)
+    value = args.rows * dist.world / (ms_step / 1e3)
+    alg = args.rows * (args.ctx * 4 + TOPK_K * 4 + 4)
+    hbm_peak, _, peak_kind = measured_peaks()
+    achieved = alg / (ms_rank / 1e3) / 1e9
+    m = None
+    prof = os.path.join(REPO, "profiles", "indexer_topk_decode.md")
+    if os.path.exists(prof) and (args.rows, args.ctx) == (32, 8192):
+        m = re.search(r"traffic_bytes_per_launch:\s*([0-9]+)", open(prof).read())
+    roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+            "frac": round(achieved / hbm_peak, 4), "peak_source": peak_kind,
+            "traffic": int(m.group(1)) if m else None, "algorithmic_bytes_per_launch": alg,
+            "note": "latency-bound: each row is a chain of dependent selection passes on one SM"}
+    # vLLM's compiled op of the same contract, timed the same way, for comparison
+    vllm_cmp = None
+    try:
+        from vllm import _custom_ops as ops
+
+        def vstep(k):
+            ops.top_k_per_row_decode(sets[k % len(sets)], 1, seq, out, args.rows, args.ctx, 1,
+                                     TOPK_K)
+        ms_v, _, _ = time_graph(vstep, args, Dist(1), device, stream)
+        vllm_cmp = {"op": "vllm._custom_ops.top_k_per_row_decode", "ms_per_step": round(ms_v, 5)}
+    except Exception as exc:   # library code, optional
+        vllm_cmp = {"unavailable": repr(exc)[:120]}
+    e2e = None
+    if not args.no_e2e:
+        hl = [x.cpu().pin_memory() for x in sets]
+        dl = [torch.empty_like(x) for x in sets]
+        back = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+
+        def e2e_step(k):
+            j = k % len(sets)
+            dl[j].copy_(hl[j], non_blocking=True)
+            G.top_k_per_row_decode(dl[j], 1, seq, out, args.rows, args.ctx, 1, TOPK_K)
+            back.copy_(out, non_blocking=True)
+
+        for k in range(max(args.warmup, 3)):
+            e2e_step(k)
+        torch.cuda.synchronize()
+        dist.barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record()
+        for k in range(args.steps):
+            e2e_step(k)
+        f1.record()
+        torch.cuda.synchronize()
+        ms_e = dist.max(f0.elapsed_time(f1), device) / args.steps
+        e2e = {"value": round(args.rows * dist.world / (ms_e / 1e3), 1), "unit": TK_UNIT,
+               "h2d_bytes_per_step": args.rows * args.ctx * 4,
+               "d2h_bytes_per_step": args.rows * TOPK_K * 4, "ms_per_step": round(ms_e, 5),
+               "path": "glm53_sparse_mla.top_k_per_row_decode (torch op -> C ABI), pinned host "
+                       "buffers"}
+    cpu = None
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        cpu = topk_cpu(sets[0].cpu().numpy(), args.ctx, args.cpu_seconds)
+    if dist.rank == 0:
+        cfg = topk_desc(args)
+        cfg.update({"parallelism": f"dp{dist.world}",
+                    "l2": f"{len(sets)} rotating logits sets "
+                          f"({len(sets) * args.rows * args.ctx * 4 / 1e6:.0f} MB); logits are "
+                          "fresh from the indexer in use, so L2-resident inputs are the "
+                          "realistic case",
+                    "timing": "K steps in one CUDA graph, CUDA events, max over ranks"})
+        line = {"metric": f"indexer top-{TOPK_K} {TK_UNIT} (decode, ctx {args.ctx})",
+                "value": round(value, 1), "unit": TK_UNIT, "n_gpus": dist.world,
+                "steps": args.steps, "warmup": max(args.warmup, 3),
+                "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)", "config": cfg,
+                "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
+                "library_comparison": vllm_cmp,
+                "gpu_launches": args.steps + (args.steps if e2e else 0), "clocks": clocks}
+        print(json.dumps(line), flush=True)
+    dist.close()
+
+
+def topk_cpu(logits: np.ndarray, ctx: int, seconds: float):
+    """The oracle's top-k timed on this host over a sample of the step."""
+    from oracle import topk_oracle as TK
+    rows = logits.shape[0]
+    done, t0 = 0, time.perf_counter()
+    while True:
+        r = done % rows
+        TK.topk_row(logits[r], 0, ctx, TOPK_K)
+        done += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(done / dt, 2), "unit": TK_UNIT, "cores": 1, "kind": "port",
+            "sample": f"{done} rows of the step, numpy oracle (restates vLLM's "
+                      f"top_k_per_row_decode), {dt:.1f} s"}
+
+
+def run_topk_reference(args, dist: Dist):
+    if dist.rank != 0:
+        return
+    sets = topk_sets(args, "cpu", 1)
+    cpu = topk_cpu(sets[0].numpy(), args.ctx, max(1.0, min(args.cpu_seconds, 30.0)))
+    line = {"impl": "reference", "metric": f"indexer top-{TOPK_K} {TK_UNIT} (decode, ctx {args.ctx})",
+            "value": cpu["value"], "unit": TK_UNIT, "n_gpus": dist.world, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+            "config": topk_desc(args), "cpu_baseline": cpu,
+            "e2e": {"value": cpu["value"], "unit": TK_UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
 
 
 def run_e2e(args, G, sets, device, dist: Dist):
@@ -697,6 +853,11 @@ def main():
             run_cache_write_reference(args, dist)
         else:
             run_cache_write(args, dist)
+    elif args.op == "topk":
+        if args.impl == "reference":
+            run_topk_reference(args, dist)
+        else:
+            run_topk(args, dist)
     elif args.impl == "reference":
         run_reference(args, dist)
     else:
