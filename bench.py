@@ -40,6 +40,8 @@ oracle port) on the host cores instead, on rank 0 only.
 feeds the attention): --tokens new tokens per step (default 8192, a
 chunked-prefill step) into a 524288-slot paged cache, --kv fp8 (default bf16)
 for the plain fp8 cache, same JSON line with its own metric and roofline.
+--op indexer measures the indexer's fp8 paged MQA logits over --rows decode
+rows of --ctx cached positions (64 heads, block 64, 8 rotating caches).
 --op topk measures the indexer's per-row top-2048 over --rows decode rows of
 --ctx logits (default 32 x 8192, C2's batch and context), with vLLM's
 compiled op of the same contract timed alongside when it loads.
@@ -74,9 +76,10 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--op", choices=["attention", "cache_write", "topk"], default="attention",
-                    help="attention (the headline), the latent KV-cache writer, or the "
-                         "indexer's per-row top-k")
+    ap.add_argument("--op", choices=["attention", "cache_write", "indexer", "topk"],
+                    default="attention",
+                    help="attention (the headline), the latent KV-cache writer, the indexer's "
+                         "fp8 paged logits, or its per-row top-k")
     ap.add_argument("--tokens", type=int, default=8192,
                     help="cache_write: new tokens per step (a chunked-prefill step)")
     ap.add_argument("--rows", type=int, default=32, help="topk: decode rows (query tokens)")
@@ -696,6 +699,162 @@ def run_topk_reference(args, dist: Dist):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# the indexer's paged fp8 MQA logits (--op indexer)
+# ---------------------------------------------------------------------------
+IDX_HEADS = 64
+IDX_BLOCK = 64
+IX_UNIT = "rows/s"
+
+
+def indexer_sets(args, device, n_sets: int, seed0: int = 700):
+    """n_sets independent decode steps: q, weights, an fp8 indexer cache of
+    rows x ctx positions (own blocks per row), block tables, lengths."""
+    g = torch.Generator(device="cpu")
+    blocks_per_row = (args.ctx + IDX_BLOCK - 1) // IDX_BLOCK
+    nb = args.rows * blocks_per_row
+    out = []
+    for s in range(n_sets):
+        g.manual_seed(seed0 + s)
+        q = torch.randn((args.rows, 1, IDX_HEADS, 128), generator=g).to(torch.float8_e4m3fn)
+        vals = torch.randn((nb, IDX_BLOCK * 128), generator=g).to(torch.float8_e4m3fn).view(torch.uint8)
+        sc = (torch.rand((nb, IDX_BLOCK), generator=g) + 0.5).view(torch.uint8)
+        cache = torch.cat([vals, sc], 1).contiguous().view(nb, IDX_BLOCK, 1, 132)
+        w = torch.randn((args.rows, IDX_HEADS), generator=g)
+        bt = torch.randperm(nb, generator=g).to(torch.int32).view(args.rows, blocks_per_row)
+        out.append(tuple(x.to(device) for x in (q, cache, w, bt)))
+    ctx = torch.full((args.rows,), args.ctx, dtype=torch.int32, device=device)
+    return out, ctx
+
+
+def indexer_bytes(args) -> int:
+    """Algorithmic bytes per launch: cache rows and scales read once, queries
+    and weights, logits written over max_model_len (= ctx here)."""
+    return args.rows * (args.ctx * 132 + IDX_HEADS * 128 + IDX_HEADS * 4 + args.ctx * 4)
+
+
+def indexer_desc(args) -> dict:
+    return {"workload": f"indexer fp8 paged MQA logits: {args.rows} decode rows x {args.ctx} "
+                        f"cached positions, {IDX_HEADS} heads x 128, block {IDX_BLOCK}",
+            "rows_per_step": args.rows, "ctx": args.ctx, "heads": IDX_HEADS}
+
+
+def run_indexer(args, dist: Dist):
+    torch.cuda.set_device(dist.local)
+    device = torch.device("cuda", dist.local)
+    dist.init("nccl")
+    import glm53_sparse_mla as G
+    sets, ctx = indexer_sets(args, device, max(1, args.sets), 700 + 1000 * dist.rank)
+    logits = torch.empty((args.rows, args.ctx), dtype=torch.float32, device=device)
+
+    def step(k):
+        q, cache, w, bt = sets[k % len(sets)]
+        G.fp8_paged_mqa_logits(q, cache, w, ctx, bt, args.ctx, logits=logits)
+
+    stream = torch.cuda.Stream(device)
+    ms_rank, ms_step, clocks = time_graph(step, args, dist, device, stream)
+    value = args.rows * dist.world / (ms_step / 1e3)
+    alg = indexer_bytes(args)
+    hbm_peak, tf_peak, peak_kind = measured_peaks()
+    achieved = alg / (ms_rank / 1e3) / 1e9
+    m = None
+    prof = os.path.join(REPO, "profiles", "indexer_logits_decode.md")
+    if os.path.exists(prof) and (args.rows, args.ctx) == (32, 8192):
+        m = re.search(r"traffic_bytes_per_launch:\s*([0-9]+)", open(prof).read())
+    flops = 2 * args.rows * args.ctx * IDX_HEADS * 128
+    roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+            "frac": round(achieved / hbm_peak, 4), "peak_source": peak_kind,
+            "traffic": int(m.group(1)) if m else None, "algorithmic_bytes_per_launch": alg,
+            "tensor_tflops_fp8": round(flops / (ms_rank / 1e3) / 1e12, 1)}
+    e2e = None
+    if not args.no_e2e:
+        hq = [s[0].cpu().pin_memory() for s in sets]
+        hw = [s[2].cpu().pin_memory() for s in sets]
+        dq = [torch.empty_like(s[0]) for s in sets]
+        dw = [torch.empty_like(s[2]) for s in sets]
+        back = torch.empty(logits.shape, dtype=logits.dtype).pin_memory()
+
+        def e2e_step(k):
+            j = k % len(sets)
+            dq[j].copy_(hq[j], non_blocking=True)
+            dw[j].copy_(hw[j], non_blocking=True)
+            G.fp8_paged_mqa_logits(dq[j], sets[j][1], dw[j], ctx, sets[j][3], args.ctx,
+                                   logits=logits)
+            back.copy_(logits, non_blocking=True)
+
+        for k in range(max(args.warmup, 3)):
+            e2e_step(k)
+        torch.cuda.synchronize()
+        dist.barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record()
+        for k in range(args.steps):
+            e2e_step(k)
+        f1.record()
+        torch.cuda.synchronize()
+        ms_e = dist.max(f0.elapsed_time(f1), device) / args.steps
+        e2e = {"value": round(args.rows * dist.world / (ms_e / 1e3), 1), "unit": IX_UNIT,
+               "h2d_bytes_per_step": args.rows * IDX_HEADS * (128 + 4),
+               "d2h_bytes_per_step": args.rows * args.ctx * 4, "ms_per_step": round(ms_e, 5),
+               "path": "glm53_sparse_mla.fp8_paged_mqa_logits (torch op -> C ABI), pinned host "
+                       "buffers; the cache is resident device state"}
+    cpu = None
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        cpu = indexer_cpu(sets[0], args, args.cpu_seconds)
+    if dist.rank == 0:
+        cfg = indexer_desc(args)
+        cfg.update({"parallelism": f"dp{dist.world}",
+                    "l2": f"{len(sets)} rotating caches, "
+                          f"{len(sets) * args.rows * args.ctx * 132 / 1e6:.0f} MB (>> 126 MB L2)",
+                    "timing": "K steps in one CUDA graph, CUDA events, max over ranks"})
+        line = {"metric": f"indexer logits {IX_UNIT} (decode, ctx {args.ctx}, {IDX_HEADS} heads)",
+                "value": round(value, 1), "unit": IX_UNIT, "n_gpus": dist.world,
+                "steps": args.steps, "warmup": max(args.warmup, 3),
+                "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "fp8_e4m3", "data": "synthetic (seeded)",
+                "config": cfg, "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
+                "gpu_launches": args.steps + (args.steps if e2e else 0), "clocks": clocks}
+        print(json.dumps(line), flush=True)
+    dist.close()
+
+
+def indexer_cpu(one_set, args, seconds: float):
+    """The oracle's logits timed on this host, one row at a time."""
+    from oracle import indexer_logits_oracle as IL
+    q, cache, w, bt = (x.cpu() for x in one_set)
+    qb = q.view(torch.uint8).numpy()
+    kv = cache.view(cache.shape[0], -1).numpy()
+    wn, btn = w.numpy(), bt.numpy()
+    done, t0 = 0, time.perf_counter()
+    while True:
+        r = done % args.rows
+        IL.paged_mqa_logits(qb[r:r + 1], kv, wn[r:r + 1], np.array([args.ctx]), btn[r:r + 1],
+                            args.ctx)
+        done += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(done / dt, 2), "unit": IX_UNIT, "cores": 1, "kind": "port",
+            "sample": f"{done} rows of the step, numpy oracle (restates vLLM's "
+                      f"fp8_paged_mqa_logits_torch), {dt:.1f} s"}
+
+
+def run_indexer_reference(args, dist: Dist):
+    if dist.rank != 0:
+        return
+    sets, _ = indexer_sets(args, "cpu", 1)
+    cpu = indexer_cpu(sets[0], args, max(1.0, min(args.cpu_seconds, 30.0)))
+    line = {"impl": "reference",
+            "metric": f"indexer logits {IX_UNIT} (decode, ctx {args.ctx}, {IDX_HEADS} heads)",
+            "value": cpu["value"], "unit": IX_UNIT, "n_gpus": dist.world, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+            "config": indexer_desc(args), "cpu_baseline": cpu,
+            "e2e": {"value": cpu["value"], "unit": IX_UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def run_e2e(args, G, sets, device, dist: Dist):
     n = len(sets)
     q_h = [w.q.cpu().pin_memory() for w in sets]
@@ -853,6 +1012,11 @@ def main():
             run_cache_write_reference(args, dist)
         else:
             run_cache_write(args, dist)
+    elif args.op == "indexer":
+        if args.impl == "reference":
+            run_indexer_reference(args, dist)
+        else:
+            run_indexer(args, dist)
     elif args.op == "topk":
         if args.impl == "reference":
             run_topk_reference(args, dist)

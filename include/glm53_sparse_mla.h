@@ -272,6 +272,48 @@ int glm53_topk_per_row(const float* logits, int64_t num_rows, int64_t stride0, i
  * Synchronises the device. Not part of the hot path. */
 int glm53_topk_status(uint32_t* status, int clear);
 
+/*
+ * Sparse-attention indexer scores over a paged fp8 cache: the logits the
+ * top-k above selects from.
+ *
+ *   q              [B, next_n, H, 128] fp8_e4m3 (H = 32 or 64, next_n = 1, 2
+ *                  or 4)
+ *   kv_cache       num_blocks blocks, block_bytes apart (a multiple of 16,
+ *                  >= block_size * 132; block_size a power of two, 16 to
+ *                  1024): block_size rows of 128 e4m3 values, then
+ *                  block_size fp32 scales
+ *   weights        [B * next_n, H] fp32
+ *   context_lens   [B] (token j of request i sees positions
+ *                  < context_lens[i] - next_n + j + 1), or with
+ *                  per_token_lens, [B * next_n] (token j sees
+ *                  < context_lens[i * next_n + j])
+ *   block_table    [B, bt_stride] int32, the first max_blocks columns used
+ *   logits         [B * next_n, logits_stride] fp32:
+ *                  logits[row, p] = scale[p] * sum_h relu(q[h] . k[p]) * w[row, h]
+ *                  on visible positions; with `clean`, -inf elsewhere up to
+ *                  max_model_len, otherwise untouched.
+ *
+ * Replaces DeepGEMM's fp8 paged MQA logits as vLLM's sparse-attention
+ * indexer calls it (vllm 0.22.0 vllm/utils/deep_gemm.py:407-456, from
+ * vllm/model_executor/layers/sparse_attn_indexer.py:324-333); the indexer's
+ * top-k then fills the topk_indices_buffer the reference's backend reads
+ * (glm53_sparse_mla/backend.py:310-314 of the reference). Positions whose
+ * block is past the table or the cache read nothing and raise a bit in
+ * glm53_indexer_status. Asynchronous on `stream`; no allocation.
+ */
+int glm53_indexer_logits(const void* q, const void* kv_cache, const float* weights,
+                         const int32_t* context_lens, int per_token_lens,
+                         const int32_t* block_table, int64_t B, int next_n, int64_t H,
+                         int64_t head_dim, int64_t num_blocks, int64_t block_size,
+                         int64_t block_bytes, int64_t bt_stride, int64_t max_blocks,
+                         float* logits, int64_t logits_stride, int64_t max_model_len, int clean,
+                         void* stream);
+
+/* Read (and optionally clear) the indexer-logits status word (1: a wait gave
+ * up after its time limit; 2: a block past the table or the cache was
+ * skipped). Synchronises the device. Not part of the hot path. */
+int glm53_indexer_status(uint32_t* status, int clear);
+
 #ifdef __cplusplus
 }
 #endif

@@ -117,6 +117,12 @@ __device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint3
                : "memory");
 }
 
+// 4-byte cp.async (L1-allocating form, the one that takes sizes below 16).
+__device__ __forceinline__ void cp_async_4(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+
 // The arrive fires once every cp.async this thread issued so far has landed;
 // .noinc makes that deferred arrive count as one of the barrier's expected
 // arrivals.
@@ -158,6 +164,18 @@ __device__ __forceinline__ void stg_v4(void* p, uint4 v) {
 // memory into L2; fire and forget, no registers or shared memory involved.
 __device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Bulk copy global -> shared by the copy engine (async proxy): both addresses
+// 16-byte aligned, `bytes` a multiple of 16, counted against the mbarrier's
+// transaction bytes.
+__device__ __forceinline__ void bulk_load_g2s(uint32_t sdst, const void* gsrc, uint32_t bytes,
+                                              uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          sdst),
+      "l"(gsrc), "r"(bytes), "r"(bar)
+      : "memory");
 }
 
 // 16-byte global store / load cached in L2 only (.cg): for data that other
@@ -300,6 +318,18 @@ __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint
       : "memory");
 }
 
+// D[tmem] (+)= A[smem desc] x B[smem desc], e4m3 inputs (K = 32 per
+// instruction), fp32 accumulate.
+__device__ __forceinline__ void umma_e4m3(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive once on `bar` when every tcgen05 op this thread issued so far is done.
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile(
@@ -426,6 +456,12 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, bool a_mn_ma
   return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn_major ? 1u : 0u) << 15) |
          ((b_mn_major ? 1u : 0u) << 16) | (static_cast<uint32_t>(N >> 3) << 17) |
          (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// Instruction descriptor for kind::f8f6f4 with e4m3 A and B (format 0) and
+// fp32 D; same field layout as idesc_bf16_f32.
+__host__ __device__ constexpr uint32_t idesc_e4m3_f32(int M, int N) {
+  return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
 // As idesc_bf16_f32 with f16 A/B (A and B format 0).

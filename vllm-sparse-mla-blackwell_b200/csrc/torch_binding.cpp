@@ -12,7 +12,9 @@
 // `concat_and_cache_mla` is the latent KV-cache write that feeds the op, with
 // the schema of vLLM's cache op of that name; `top_k_per_row_decode` /
 // `top_k_per_row_prefill` produce the top-k positions from the indexer's
-// logits with the schemas of vLLM's ops of those names.
+// logits with the schemas of vLLM's ops of those names, and
+// `fp8_paged_mqa_logits` computes those logits over the paged fp8 indexer
+// cache (DeepGEMM's contract as vLLM calls it).
 
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
@@ -265,6 +267,55 @@ void top_k_per_row_prefill(const torch::Tensor& logits, const torch::Tensor& cu_
            raw_topk_indices, num_rows, stride0, stride1, topk_tokens);
 }
 
+// Indexer scores with the contract of DeepGEMM's fp8 paged MQA logits as
+// vLLM 0.22.0 calls it (vllm/utils/deep_gemm.py:407-456): q [B, next_n, H, 128]
+// fp8_e4m3, kv_cache [num_blocks, block_size, (1,) 132] uint8 (128 e4m3
+// values per row, then the block's fp32 scales), weights [B * next_n, H] fp32,
+// context_lens [B] or [B, next_n] int32 (the latter per token), block_tables
+// [B, max_blocks] int32; writes logits [B * next_n, >= max_model_len] fp32.
+void fp8_paged_mqa_logits(const torch::Tensor& q, const torch::Tensor& kv_cache,
+                          const torch::Tensor& weights, const torch::Tensor& context_lens,
+                          const torch::Tensor& block_tables, int64_t max_model_len,
+                          bool clean_logits, torch::Tensor& logits) {
+  TORCH_CHECK(q.is_cuda() && kv_cache.is_cuda() && weights.is_cuda() && context_lens.is_cuda() &&
+                  block_tables.is_cuda() && logits.is_cuda(),
+              "glm53_sparse_mla: indexer tensors must be CUDA tensors");
+  TORCH_CHECK(q.dim() == 4 && q.is_contiguous() &&
+                  (q.scalar_type() == torch::kFloat8_e4m3fn || q.scalar_type() == torch::kUInt8),
+              "glm53_sparse_mla: q must be a contiguous fp8_e4m3 tensor [B, next_n, H, 128]");
+  const int64_t B = q.size(0), next_n = q.size(1), H = q.size(2);
+  TORCH_CHECK(q.size(3) == 128, "glm53_sparse_mla: the indexer head dim must be 128");
+  TORCH_CHECK(kv_cache.scalar_type() == torch::kUInt8 && (kv_cache.dim() == 3 || kv_cache.dim() == 4) &&
+                  kv_cache.size(-1) == 132 && kv_cache.stride(-1) == 1 &&
+                  kv_cache.stride(1) == (kv_cache.dim() == 4 ? kv_cache.size(2) * 132 : 132),
+              "glm53_sparse_mla: kv_cache must be uint8 [num_blocks, block_size, (1,) 132] with "
+              "contiguous blocks");
+  TORCH_CHECK(weights.scalar_type() == torch::kFloat && weights.is_contiguous() &&
+                  weights.dim() == 2 && weights.size(0) == B * next_n && weights.size(1) == H,
+              "glm53_sparse_mla: weights must be contiguous float32 [B * next_n, H]");
+  TORCH_CHECK(context_lens.scalar_type() == torch::kInt && context_lens.is_contiguous() &&
+                  context_lens.size(0) == B && (context_lens.dim() == 1 ||
+                  (context_lens.dim() == 2 && (context_lens.size(1) == 1 || context_lens.size(1) == next_n))),
+              "glm53_sparse_mla: context_lens must be int32 [B] or [B, next_n]");
+  TORCH_CHECK(block_tables.scalar_type() == torch::kInt && block_tables.dim() == 2 &&
+                  block_tables.size(0) >= B && block_tables.stride(1) == 1,
+              "glm53_sparse_mla: block_tables must be int32 [B, max_blocks] with contiguous rows");
+  TORCH_CHECK(logits.scalar_type() == torch::kFloat && logits.dim() == 2 &&
+                  logits.size(0) >= B * next_n && logits.size(1) >= max_model_len && logits.stride(1) == 1,
+              "glm53_sparse_mla: logits must be float32 [B * next_n, >= max_model_len]");
+  const bool per_token = context_lens.dim() == 2 && context_lens.size(1) == next_n && next_n > 1;
+  if (B == 0 || max_model_len == 0) return;
+  const c10::cuda::CUDAGuard guard(q.device());
+  cudaStream_t stream = c10::cuda::getCurrentCUDAStream(q.get_device()).stream();
+  const int rc = glm53_indexer_logits(
+      q.data_ptr(), kv_cache.data_ptr(), weights.data_ptr<float>(), context_lens.data_ptr<int32_t>(),
+      per_token ? 1 : 0, block_tables.data_ptr<int32_t>(), B, static_cast<int>(next_n), H, 128,
+      kv_cache.size(0), kv_cache.size(1), kv_cache.stride(0), block_tables.stride(0),
+      block_tables.size(1), logits.data_ptr<float>(), logits.stride(0), max_model_len,
+      clean_logits ? 1 : 0, static_cast<void*>(stream));
+  TORCH_CHECK(rc == GLM53_OK, "glm53_sparse_mla: ", glm53_sparse_mla_strerror(rc));
+}
+
 TORCH_LIBRARY(glm53_sparse_mla, m) {
   m.def("sparse_fwd(Tensor q, Tensor kv, Tensor indices, float sm_scale, float kv_scale, Tensor(a!) out) -> ()");
   m.def("sparse_fwd_lse(Tensor q, Tensor kv, Tensor indices, float sm_scale, float kv_scale, Tensor(a!) out, Tensor(b!) lse) -> ()");
@@ -272,6 +323,7 @@ TORCH_LIBRARY(glm53_sparse_mla, m) {
   m.def("concat_and_cache_mla(Tensor kv_c, Tensor k_pe, Tensor(a!) kv_cache, Tensor slot_mapping, str kv_cache_dtype, Tensor scale) -> ()");
   m.def("top_k_per_row_decode(Tensor logits, int next_n, Tensor seq_lens, Tensor(a!) raw_topk_indices, int num_rows, int stride0, int stride1, int topk_tokens) -> ()");
   m.def("top_k_per_row_prefill(Tensor logits, Tensor cu_seqlen_ks, Tensor cu_seqlen_ke, Tensor(a!) raw_topk_indices, int num_rows, int stride0, int stride1, int topk_tokens) -> ()");
+  m.def("fp8_paged_mqa_logits(Tensor q, Tensor kv_cache, Tensor weights, Tensor context_lens, Tensor block_tables, int max_model_len, bool clean_logits, Tensor(a!) logits) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(glm53_sparse_mla, CUDA, m) {
@@ -281,4 +333,5 @@ TORCH_LIBRARY_IMPL(glm53_sparse_mla, CUDA, m) {
   m.impl("concat_and_cache_mla", &concat_and_cache_mla);
   m.impl("top_k_per_row_decode", &top_k_per_row_decode);
   m.impl("top_k_per_row_prefill", &top_k_per_row_prefill);
+  m.impl("fp8_paged_mqa_logits", &fp8_paged_mqa_logits);
 }

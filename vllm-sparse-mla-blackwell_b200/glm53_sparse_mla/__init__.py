@@ -26,6 +26,8 @@ __all__ = [
     "concat_and_cache_mla",
     "top_k_per_row_decode",
     "top_k_per_row_prefill",
+    "fp8_paged_mqa_logits",
+    "fp8_fp4_paged_mqa_logits",
     "HEADS_PER_RANK",
     "SUPPORTED_HEADS_PER_RANK",
     "KV_LORA_RANK",
@@ -184,6 +186,41 @@ def top_k_per_row_prefill(logits, cu_seqlen_ks, cu_seqlen_ke, raw_topk_indices, 
         int(stride1), int(topk_tokens))
 
 
+def fp8_paged_mqa_logits(q, kv_cache, weights, context_lens, block_tables, max_model_len,
+                         clean_logits=True, logits=None):
+    """The sparse-attention indexer's scores over its paged fp8 cache.
+
+    q [B, next_n, H, 128] fp8_e4m3 (H 32 or 64, next_n 1, 2 or 4); kv_cache
+    [num_blocks, block_size, (1,) 132] uint8 (each block: block_size rows of
+    128 e4m3 values, then block_size fp32 scales); weights [B * next_n, H]
+    fp32; context_lens [B] (token j of request i sees positions
+    < context_lens[i] - next_n + j + 1) or [B, next_n] (per token);
+    block_tables [B, max_blocks] int32. Returns logits [B * next_n,
+    max_model_len] fp32: scale[p] * sum_h relu(q[h] . k[p]) * w[h] on visible
+    positions, -inf elsewhere with ``clean_logits`` (untouched without it).
+    """
+    if logits is None:
+        logits = torch.empty((q.shape[0] * q.shape[1], int(max_model_len)), dtype=torch.float32,
+                             device=q.device)
+    torch.ops.glm53_sparse_mla.fp8_paged_mqa_logits(q, kv_cache, weights, context_lens,
+                                                    block_tables, int(max_model_len),
+                                                    bool(clean_logits), logits)
+    return logits
+
+
+def fp8_fp4_paged_mqa_logits(q, kv_cache, weights, context_lens, block_tables,
+                             schedule_metadata, max_model_len, clean_logits):
+    """Drop-in for vLLM's ``vllm.utils.deep_gemm.fp8_fp4_paged_mqa_logits``
+    (vllm 0.22.0 vllm/utils/deep_gemm.py:407-456) on the fp8 path: ``q`` is
+    the ``(values, None)`` pair; ``schedule_metadata`` (DeepGEMM's SM
+    schedule) is not needed and ignored."""
+    values, q_scale = q if isinstance(q, tuple) else (q, None)
+    if q_scale is not None:
+        raise NotImplementedError("glm53_sparse_mla: the MXFP4 indexer cache is not supported")
+    return fp8_paged_mqa_logits(values, kv_cache, weights, context_lens, block_tables,
+                                max_model_len, clean_logits)
+
+
 # Shape-only meta kernels so torch.compile can trace through the ops.
 @torch.library.register_fake("glm53_sparse_mla::sparse_fwd")
 def _sparse_fwd_fake(q, kv, indices, sm_scale, kv_scale, out):
@@ -225,4 +262,11 @@ def _top_k_per_row_decode_fake(logits, next_n, seq_lens, raw_topk_indices, num_r
 def _top_k_per_row_prefill_fake(logits, cu_seqlen_ks, cu_seqlen_ke, raw_topk_indices, num_rows,
                                 stride0, stride1, topk_tokens):
     torch._check(raw_topk_indices.dim() == 2)
+    return None
+
+
+@torch.library.register_fake("glm53_sparse_mla::fp8_paged_mqa_logits")
+def _fp8_paged_mqa_logits_fake(q, kv_cache, weights, context_lens, block_tables, max_model_len,
+                               clean_logits, logits):
+    torch._check(q.dim() == 4 and logits.dim() == 2)
     return None

@@ -42,8 +42,9 @@ NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "--expt-relaxed-constexpr",
               "-Xcompiler", "-fPIC", "-Xptxas", "--warn-on-spills"]
 
 LIB_NAME = "libglm53_sparse_mla.so"
-# attention kernel + host launcher; latent KV-cache writer; indexer top-k
-KERNEL_SOURCES = ["sparse_mla_sm100.cu", "kv_cache_writer_sm100.cu", "topk_sm100.cu"]
+# attention kernel + host launcher; latent KV-cache writer; indexer scores and top-k
+KERNEL_SOURCES = ["sparse_mla_sm100.cu", "kv_cache_writer_sm100.cu", "indexer_logits_sm100.cu",
+                  "topk_sm100.cu"]
 OP_NAME = "_C.so"
 
 
