@@ -117,6 +117,10 @@ class Dist:
 
     def init(self, backend: str):
         if self.world > 1:
+            # NCCL's version banner (NCCL_DEBUG=VERSION) would precede the one
+            # JSON line rank 0 prints; warnings and above still show
+            if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+                os.environ["NCCL_DEBUG"] = "WARN"
             import datetime
             torch.distributed.init_process_group(
                 backend, timeout=datetime.timedelta(seconds=180),
