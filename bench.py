@@ -98,6 +98,7 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--no-spread", action="store_true", help="skip the median / p10 / p90 replays")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     return ap.parse_args()
 
@@ -355,6 +356,32 @@ def run_ours(args, dist: Dist):
     del graph
     torch.cuda.synchronize()
 
+    # spread (outside the contract's one timed run): 20 replays of a graph of
+    # up to 50 steps, each timed, give median and p10 / p90 per step
+    spread = None
+    if not args.no_spread:
+        n_sp = min(50, args.steps)
+        g_sp = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_sp, stream=stream):
+            for k in range(n_sp):
+                step(k)
+        torch.cuda.synchronize()
+        per = []
+        for _ in range(20):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
+                a.record(stream)
+                g_sp.replay()
+                b.record(stream)
+            b.synchronize()
+            per.append(a.elapsed_time(b) / n_sp)
+        del g_sp
+        torch.cuda.synchronize()
+        q = np.percentile(per, [10, 50, 90])
+        spread = {"median_ms": round(float(q[1]), 5), "p10_ms": round(float(q[0]), 5),
+                  "p90_ms": round(float(q[2]), 5), "replays": 20, "steps_per_replay": n_sp,
+                  "rank": dist.rank}
+
     # end to end through the public API with host buffers
     e2e = None
     if not args.no_e2e:
@@ -382,7 +409,7 @@ def run_ours(args, dist: Dist):
                 "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, random init)",
                 "config": cfg, "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
                 "gpu_launches": args.steps + (args.steps if e2e else 0),
-                "clocks": clk.summary()}
+                "clocks": clk.summary(), "spread": spread}
         print(json.dumps(line), flush=True)
     dist.close()
 
