@@ -46,6 +46,8 @@ chunked-prefill step) into a 524288-slot paged cache, --kv fp8 (default bf16)
 for the plain fp8 cache, same JSON line with its own metric and roofline.
 --op indexer measures the indexer's fp8 paged MQA logits over --rows decode
 rows of --ctx cached positions (64 heads, block 64, 8 rotating caches).
+--op decode_step chains the four (cache write, indexer logits, top-2048,
+paged attention) as one sparse decode step of --rows sequences at --ctx.
 --op topk measures the indexer's per-row top-2048 over --rows decode rows of
 --ctx logits (default 32 x 8192, C2's batch and context), with vLLM's
 compiled op of the same contract timed alongside when it loads.
@@ -80,10 +82,11 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--op", choices=["attention", "cache_write", "indexer", "topk"],
+    ap.add_argument("--op", choices=["attention", "cache_write", "indexer", "topk", "decode_step"],
                     default="attention",
                     help="attention (the headline), the latent KV-cache writer, the indexer's "
-                         "fp8 paged logits, or its per-row top-k")
+                         "fp8 paged logits, its per-row top-k, or the four chained as one "
+                         "sparse decode step")
     ap.add_argument("--tokens", type=int, default=8192,
                     help="cache_write: new tokens per step (a chunked-prefill step)")
     ap.add_argument("--rows", type=int, default=32, help="topk: decode rows (query tokens)")
@@ -890,6 +893,79 @@ def run_indexer_reference(args, dist: Dist):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# the whole sparse decode step (--op decode_step)
+# ---------------------------------------------------------------------------
+def decode_step_sets(args, device, n_sets: int, seed0: int = 900):
+    """Per set: a paged bf16 latent cache and an fp8 indexer cache sharing one
+    block table (rows x ctx positions, block 64), plus the step's inputs: each
+    request's new latent row, indexer queries and weights, attention queries."""
+    g = torch.Generator(device="cpu")
+    bpr = (args.ctx + IDX_BLOCK - 1) // IDX_BLOCK
+    nb = args.rows * bpr
+    out = []
+    for s in range(n_sets):
+        g.manual_seed(seed0 + s)
+        bt = torch.randperm(nb, generator=g).to(torch.int32).view(args.rows, bpr)
+        lat = (torch.randn((nb, IDX_BLOCK, 512), generator=g) * 0.5).to(torch.bfloat16)
+        vals = torch.randn((nb, IDX_BLOCK * 128), generator=g).to(torch.float8_e4m3fn).view(torch.uint8)
+        sc = (torch.rand((nb, IDX_BLOCK), generator=g) + 0.5).view(torch.uint8)
+        icache = torch.cat([vals, sc], 1).contiguous().view(nb, IDX_BLOCK, 1, 132)
+        qi = torch.randn((args.rows, 1, IDX_HEADS, 128), generator=g).to(torch.float8_e4m3fn)
+        w = torch.randn((args.rows, IDX_HEADS), generator=g)
+        q = torch.randn((args.rows, 64, 512), generator=g).to(torch.bfloat16)
+        kv_new = torch.randn((args.rows, 512), generator=g).to(torch.bfloat16)
+        # the new token of request r sits at position ctx - 1 of its table
+        last = args.ctx - 1
+        slots = (bt[:, last // IDX_BLOCK].to(torch.int64) * IDX_BLOCK + last % IDX_BLOCK)
+        out.append({k: v.to(device) for k, v in dict(
+            bt=bt, lat=lat, icache=icache, qi=qi, w=w, q=q, kv_new=kv_new, slots=slots).items()})
+    return out
+
+
+def run_decode_step(args, dist: Dist):
+    torch.cuda.set_device(dist.local)
+    device = torch.device("cuda", dist.local)
+    dist.init("nccl")
+    import glm53_sparse_mla as G
+    sets = decode_step_sets(args, device, max(1, min(args.sets, 3)), 900 + 1000 * dist.rank)
+    ctx = torch.full((args.rows,), args.ctx, dtype=torch.int32, device=device)
+    req = torch.arange(args.rows, dtype=torch.int32, device=device)
+    logits = torch.empty((args.rows, args.ctx), dtype=torch.float32, device=device)
+    pos = torch.empty((args.rows, TOPK_K), dtype=torch.int32, device=device)
+    out = torch.empty((args.rows, 64, 512), dtype=torch.bfloat16, device=device)
+    one = torch.ones(1, dtype=torch.float32, device=device)
+
+    def step(k):
+        d = sets[k % len(sets)]
+        G.concat_and_cache_mla(d["kv_new"], d["kv_new"][:, :0], d["lat"], d["slots"], "auto", one)
+        G.fp8_paged_mqa_logits(d["qi"], d["icache"], d["w"], ctx, d["bt"], args.ctx, logits=logits)
+        G.top_k_per_row_decode(logits, 1, ctx, pos, args.rows, args.ctx, 1, TOPK_K)
+        G.sparse_fwd_paged(d["q"], d["lat"].view(-1, 512), pos, req, d["bt"], IDX_BLOCK,
+                           512 ** -0.5, out=out)
+
+    stream = torch.cuda.Stream(device)
+    ms_rank, ms_step, clocks = time_graph(step, args, dist, device, stream)
+    value = args.rows * dist.world / (ms_step / 1e3)
+    if dist.rank == 0:
+        line = {"metric": f"sparse decode step query-tokens/s (cache write + indexer logits + "
+                          f"top-{TOPK_K} + attention, ctx {args.ctx}, 64 heads)",
+                "value": round(value, 1), "unit": UNIT, "n_gpus": dist.world,
+                "steps": args.steps, "warmup": max(args.warmup, 3),
+                "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16 attention, fp8 indexer",
+                "data": "synthetic (seeded)",
+                "config": {"workload": f"{args.rows} decode sequences x {args.ctx} cached tokens: "
+                                       "latent cache write (bf16), indexer fp8 paged logits "
+                                       f"({IDX_HEADS} heads), top-{TOPK_K}, paged sparse-MLA "
+                                       "attention (64 heads) on the top-k positions",
+                           "rows": args.rows, "ctx": args.ctx, "parallelism": f"dp{dist.world}",
+                           "timing": "K steps in one CUDA graph, CUDA events, max over ranks"},
+                "gpu_launches": 4 * args.steps, "clocks": clocks}
+        print(json.dumps(line), flush=True)
+    dist.close()
+
+
 def run_e2e(args, G, sets, device, dist: Dist):
     n = len(sets)
     q_h = [w.q.cpu().pin_memory() for w in sets]
@@ -1060,6 +1136,13 @@ def main():
             run_cache_write_reference(args, dist)
         else:
             run_cache_write(args, dist)
+    elif args.op == "decode_step":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the reference has no CPU "
+                              "implementation of the indexer or the cache writer; its arms are "
+                              "--op attention, cache_write, indexer and topk"}), flush=True)
+        else:
+            run_decode_step(args, dist)
     elif args.op == "indexer":
         if args.impl == "reference":
             run_indexer_reference(args, dist)
