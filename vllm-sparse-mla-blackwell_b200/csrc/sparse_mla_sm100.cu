@@ -78,26 +78,41 @@ constexpr int kTmemCols = 512;
 constexpr uint32_t kTmemS = 256;    // S double buffer at columns 256 and 320
 constexpr float kRescaleThreshold = 8.0f;   // log2 units: rescale when max grows > 256x
 
-// Shared-memory map (byte offsets from a 1024-aligned base).
-constexpr uint32_t kSmQ = 0;                          // 64 rows x 512 bf16 = 64 KB
-constexpr uint32_t kStageBytes = 65536;               // 64 rows x 512 bf16
-constexpr uint32_t kSmKV = 65536;                     // 2 stages; reused for the fp32 partial
-constexpr uint32_t kPBytes = 8192;                    // NH rows x 128 B, NH <= 64
-constexpr uint32_t kSmP = kSmKV + 2 * kStageBytes;    // 2 P buffers
-constexpr uint32_t kSmIdx = kSmP + 2 * kPBytes;       // int32[kMaxChunk]
-constexpr uint32_t kSmHead = kSmIdx + 4 * kMaxChunk;  // m[64] l[64] alpha[64] f[64]
-constexpr uint32_t kSmBar = kSmHead + 4 * 64 * 4;     // mbarriers
-constexpr uint32_t kSmMisc = kSmBar + 16 * 8;         // tmem base, counts, abort flag
-constexpr uint32_t kSmMlRecv = kSmMisc + 64;         // m[8][64], l[8][64] of the split peers
-constexpr uint32_t kSmUsed = kSmMlRecv + 2 * 8 * 64 * 4;
-constexpr uint32_t kSmemBytes = kSmUsed + 1024;       // + slack to align the base
+constexpr uint32_t kStageBytes = 65536;   // one KV tile: 64 rows x 512 bf16 (or f16)
+
+// Shared-memory map (byte offsets from a 1024-aligned base), per padded head
+// count. Q is GEMM1's M = 64 A operand, stored in 64-element column blocks
+// (kQRows x 128 B each). At 32 and 64 heads it keeps all 64 rows (rows >= H
+// zero). At 16 heads only its 16 rows are stored: the UMMA's rows 16-63 then
+// read whatever follows (the next column blocks, the first 6 KB of KV stage
+// 0), which only produces S rows of heads that do not exist and that nothing
+// reads. The 48 KB this saves, with 2 KB P buffers, hold a third KV stage.
+template <int NH>
+struct Lay {
+  static constexpr int kStages = NH == 16 ? 3 : 2;
+  static constexpr uint32_t kQRows = NH == 16 ? 16 : 64;
+  static constexpr uint32_t kQBlock = kQRows * 128;                // one column block of Q
+  static constexpr uint32_t kSmQ = 0;
+  static constexpr uint32_t kSmKV = 8 * kQBlock;                   // stages; reused by the merge
+  static constexpr uint32_t kPBytes = NH == 16 ? 2048 : 8192;       // NH (<= 64) rows x 128 B
+  static constexpr uint32_t kSmP = kSmKV + kStages * kStageBytes;  // 2 P buffers
+  static constexpr uint32_t kSmIdx = kSmP + 2 * kPBytes;           // int32[kMaxChunk]
+  static constexpr uint32_t kSmHead = kSmIdx + 4 * kMaxChunk;      // m[64] l[64] alpha[64] f[64]
+  static constexpr uint32_t kSmBar = kSmHead + 4 * 64 * 4;         // mbarriers
+  static constexpr uint32_t kSmMisc = kSmBar + 16 * 8;             // tmem base, counts, abort flag
+  static constexpr uint32_t kSmMlRecv = kSmMisc + 64;              // m[8][64], l[8][64] of the peers
+  static constexpr uint32_t kSmUsed = kSmMlRecv + 2 * 8 * 64 * 4;
+  static constexpr uint32_t kSmemBytes = kSmUsed + 1024;           // + slack to align the base
+  static_assert(kSmemBytes <= 232448, "shared memory per block");
+  static_assert(kSmKV % 1024 == 0 && kSmP % 1024 == 0, "swizzle atoms need 1024-byte bases");
+};
 
 // mbarrier slots
 enum : int {
-  kBarKvFull = 0,    // [2] producers -> GEMM1 issuer: stage of tile >= 2 loaded
-  kBarKvEmpty = 2,   // [2] GEMM2 (4 commits) -> producers: stage consumed
-  kBarSFull = 4,     // [2] GEMM1 (commit) -> softmax: S ready
-  kBarSEmpty = 6,    // [2] softmax -> GEMM1 issuer: S buffer read
+  kBarKvFull = 0,    // [stages] producers -> GEMM1 issuer: stage of tile >= 2 loaded
+  kBarKvEmpty = 3,   // [stages] GEMM2 (4 commits) -> producers: stage consumed
+  kBarSFull = 6,     // [2] GEMM1 (commit) -> softmax: S ready
+  kBarSEmpty = 8,    // [2] softmax -> GEMM1 issuer: S buffer read
   kBarODone = 10,    // GEMM2 (4 commits) -> softmax: a GEMM2 finished
   kBarDrain = 11,    // GEMM1 issuer's UMMAs all retired
   kBarQFull = 12,    // all threads (cp.async) -> GEMM1 issuer: Q landed
@@ -133,10 +148,11 @@ struct Params {
 
 __device__ unsigned int g_device_status = 0;
 
+template <uint32_t kBlock = 8192>
 __device__ __forceinline__ uint32_t swz(uint32_t row, uint32_t chunk) {
   // byte offset of 16-byte chunk `chunk` (0..63) of row `row` in a tile of
-  // 64-element column blocks, each block (rows x 128 B) 8192 B apart
-  return (chunk >> 3) * 8192u + row * 128u + (((chunk & 7u) ^ (row & 7u)) << 4);
+  // 64-element column blocks, each block (rows x 128 B) kBlock bytes apart
+  return (chunk >> 3) * kBlock + row * 128u + (((chunk & 7u) ^ (row & 7u)) << 4);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -183,6 +199,14 @@ __device__ __forceinline__ void store_pairs_n(__nv_bfloat16* o_tok, int H, int d
 template <int NH, bool kFp8>
 __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __grid_constant__ Params p) {
   static_assert(NH == 16 || NH == 32 || NH == 64, "padded head count");
+  using L = Lay<NH>;
+  constexpr int kStages = L::kStages;
+  constexpr uint32_t kSmQ = L::kSmQ, kSmKV = L::kSmKV, kSmP = L::kSmP, kPBytes = L::kPBytes;
+  constexpr uint32_t kSmIdx = L::kSmIdx, kSmHead = L::kSmHead, kSmBar = L::kSmBar;
+  constexpr uint32_t kSmMisc = L::kSmMisc, kSmMlRecv = L::kSmMlRecv;
+  constexpr uint32_t kQRows = L::kQRows, kQBlock = L::kQBlock;
+  // KV ring slot of tile t (S and P stay double-buffered: t & 1)
+  auto stage_of = [](int t) -> int { return kStages == 2 ? (t & 1) : t % kStages; };
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t sb = (raw + 1023u) & ~1023u;
@@ -206,9 +230,11 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
 
   // ------------------------------------------------------------------ setup
   if (tid == 0) {
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kStages; ++s) {
       mbar_init(bar(kBarKvFull + s), kProducerThreads);
       mbar_init(bar(kBarKvEmpty + s), 4);
+    }
+    for (int s = 0; s < 2; ++s) {
       mbar_init(bar(kBarSFull + s), 1);
       mbar_init(bar(kBarSEmpty + s), 128);
     }
@@ -266,14 +292,14 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
     if (lane == 0) misc[kMiscWarpCount + warp] = static_cast<uint32_t>(cnt);
     if (bad) atomicOr(&g_device_status, static_cast<unsigned>(GLM53_DEV_BAD_INDEX));
   }
-  // Q (all 64 rows of the M=64 operand; rows >= H are zero), issued after
+  // Q (the kQRows stored rows of the M=64 operand; rows >= H are zero), issued after
   // the index loads so those are not queued behind it; its arrival is tracked
   // by its own barrier so the KV gather never waits on it.
   // bf16 KV: Q by cp.async as it is. fp8 KV (f16 datapath): Q through
   // registers, converted to f16 with one power-of-two scale s_q per token
   // that puts max |q * s_q| in [2^13, 2^14): exact for every bf16 value in
   // range, never overflowing; 1 / s_q is folded into the softmax scale.
-  constexpr int kQPer = (64 * 64 + kThreads - 1) / kThreads;
+  constexpr int kQPer = (kQRows * 64 + kThreads - 1) / kThreads;
   uint4 qv[kFp8 ? kQPer : 1];
   float s_q = 1.f;
   if constexpr (kFp8) {
@@ -283,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
     for (int i = 0; i < kQPer; ++i) {
       const int u = tid + i * kThreads;
       const int h = u >> 6, c = u & 63;
-      qv[i] = (u < 64 * 64 && h < p.H) ? ldg_nc_v4(qtok + h * kDim + c * 8) : make_uint4(0u, 0u, 0u, 0u);
+      qv[i] = (u < kQRows * 64 && h < p.H) ? ldg_nc_v4(qtok + h * kDim + c * 8) : make_uint4(0u, 0u, 0u, 0u);
       const uint32_t w4[4] = {qv[i].x, qv[i].y, qv[i].z, qv[i].w};
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
@@ -296,10 +322,10 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
     if (lane == 0) alpha_sm[warp] = qmax;   // alpha_sm is free until the softmax
   } else {
     const __nv_bfloat16* qtok = p.q + static_cast<size_t>(token) * p.H * kDim;
-    for (int u = tid; u < 64 * 64; u += kThreads) {
+    for (int u = tid; u < kQRows * 64; u += kThreads) {
       const int h = u >> 6, c = u & 63;
       const bool ok = h < p.H;
-      cp_async_16(sb + kSmQ + swz(h, c), qtok + (ok ? h : 0) * kDim + c * 8, ok ? 16u : 0u);
+      cp_async_16(sb + kSmQ + swz<kQBlock>(h, c), qtok + (ok ? h : 0) * kDim + c * 8, ok ? 16u : 0u);
     }
     cp_async_mbar_arrive_noinc(bar(kBarQFull));
   }
@@ -314,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
 #pragma unroll
     for (int i = 0; i < kQPer; ++i) {
       const int u = tid + i * kThreads;
-      if (u < 64 * 64) {
+      if (u < kQRows * 64) {
         const uint32_t w4[4] = {qv[i].x, qv[i].y, qv[i].z, qv[i].w};
         uint32_t o4[4];
 #pragma unroll
@@ -322,7 +348,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
           const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w4[k]));
           o4[k] = pack_f16x2(f.x * s_q, f.y * s_q);
         }
-        sts_v4(sb + kSmQ + swz(u >> 6, u & 63), make_uint4(o4[0], o4[1], o4[2], o4[3]));
+        sts_v4(sb + kSmQ + swz<kQBlock>(u >> 6, u & 63), make_uint4(o4[0], o4[1], o4[2], o4[3]));
       }
     }
     fence_proxy_async_smem();
@@ -364,14 +390,15 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
                                     : idesc_bf16_f32(128, NH, true, false);
   constexpr int kSteps1 = kDim / 16;          // 32
   auto gemm1_step = [=](int t, int kk) {
-    const uint32_t stage = sb + kSmKV + (t & 1) * kStageBytes;
+    const uint32_t stage = sb + kSmKV + stage_of(t) * kStageBytes;
     const uint32_t off = (kk >> 2) * 8192u + (kk & 3) * 32u;
-    umma_bf16(tmem + kTmemS + 64u * (t & 1), sdesc_sw128(sb + kSmQ + off, 16, 1024),
+    const uint32_t qoff = (kk >> 2) * kQBlock + (kk & 3) * 32u;
+    umma_bf16(tmem + kTmemS + 64u * (t & 1), sdesc_sw128(sb + kSmQ + qoff, 16, 1024),
               sdesc_sw128(stage + off, 16, 1024), kIdesc1, kk > 0 ? 1u : 0u);
   };
   auto gemm2_step = [=](int t, int i) {
     const int kk = i >> 2, m = i & 3;
-    const uint32_t stage = sb + kSmKV + (t & 1) * kStageBytes;
+    const uint32_t stage = sb + kSmKV + stage_of(t) * kStageBytes;
     const uint32_t pbuf = sb + kSmP + (t & 1) * kPBytes;
     umma_bf16(tmem + static_cast<uint32_t>(m * NH),
               sdesc_sw128(stage + m * 16384u + kk * 2048u, 8192, 1024),
@@ -387,7 +414,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
   // fp8 after a proxy fence.
   auto gather_rows = [&](int t, int r0, auto step_c, uint32_t full) {
     constexpr int kStep = decltype(step_c)::value;
-    const uint32_t stage = sb + kSmKV + (t & 1) * kStageBytes;
+    const uint32_t stage = sb + kSmKV + stage_of(t) * kStageBytes;
     const int rows = min(kRows, n_valid - kRows * t);
     if constexpr (!kFp8) {
       const uint8_t* kvb = static_cast<const uint8_t*>(p.kv);
@@ -482,7 +509,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
       }
     };
     auto store_tile = [&](int t) {
-      const uint32_t stage = sb + kSmKV + (t & 1) * kStageBytes;
+      const uint32_t stage = sb + kSmKV + stage_of(t) * kStageBytes;
 #pragma unroll
       for (int j = 0; j < kPer; ++j) {
         const int r = pw + kProducerWarps * j;
@@ -497,12 +524,14 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
         }
       }
       fence_proxy_async_smem();
-      mbar_arrive(bar(kBarKvFull + (t & 1)));
+      mbar_arrive(bar(kBarKvFull + stage_of(t)));
     };
     if constexpr (kFp8) {
       if (n_tiles > 2) load_tile(2);
       for (int t = 2; t < n_tiles; ++t) {
-        if (!mbar_wait_bounded(bar(kBarKvEmpty + (t & 1)), ((t >> 1) - 1) & 1, abort_flag, p.timeout_ns))
+        // a stage's first tile (t < kStages) needs no wait
+        if (t >= kStages && !mbar_wait_bounded(bar(kBarKvEmpty + stage_of(t)), ((t / kStages) - 1) & 1,
+                                               abort_flag, p.timeout_ns))
           break;
         store_tile(t);
         if (t + 1 < n_tiles) load_tile(t + 1);
@@ -519,9 +548,10 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
       };
       if (n_tiles > 2) prefetch_tile(2);
       for (int t = 2; t < n_tiles; ++t) {
-        if (!mbar_wait_bounded(bar(kBarKvEmpty + (t & 1)), ((t >> 1) - 1) & 1, abort_flag, p.timeout_ns))
+        if (t >= kStages && !mbar_wait_bounded(bar(kBarKvEmpty + stage_of(t)), ((t / kStages) - 1) & 1,
+                                               abort_flag, p.timeout_ns))
           break;
-        gather_rows(t, pw, std::integral_constant<int, kProducerWarps>{}, bar(kBarKvFull + (t & 1)));
+        gather_rows(t, pw, std::integral_constant<int, kProducerWarps>{}, bar(kBarKvFull + stage_of(t)));
         if (t + 1 < n_tiles) prefetch_tile(t + 1);
       }
     }
@@ -534,8 +564,11 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
     if (lane == 0) {
       bool ok = n_tiles == 0 || mbar_wait_bounded(bar(kBarQFull), 0, abort_flag, p.timeout_ns);
       for (int g1 = 0; ok && g1 < n_tiles; ++g1) {
+        // tiles 0 and 1 arrive on kBarKvFirst, so KvFull of stages 0 and 1
+        // completes first for tile kStages and kStages + 1
+        const int use = g1 / kStages - (stage_of(g1) < 2 ? 1 : 0);
         ok = (g1 < 2 ? mbar_wait_bounded(bar(kBarKvFirst + g1), 0, abort_flag, p.timeout_ns)
-                     : mbar_wait_bounded(bar(kBarKvFull + (g1 & 1)), ((g1 >> 1) - 1) & 1, abort_flag,
+                     : mbar_wait_bounded(bar(kBarKvFull + stage_of(g1)), use & 1, abort_flag,
                                          p.timeout_ns)) &&
              (g1 < 2 ||
               mbar_wait_bounded(bar(kBarSEmpty + (g1 & 1)), ((g1 >> 1) - 1) & 1, abort_flag, p.timeout_ns));
@@ -645,7 +678,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) gemm2_step(t, 4 * kk + warp);
-        umma_commit(bar(kBarKvEmpty + b));
+        umma_commit(bar(kBarKvEmpty + stage_of(t)));
         umma_commit(bar(kBarODone));
       }
       __syncwarp();
@@ -872,10 +905,12 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
     float* const scal = reinterpret_cast<float*>(gb + kSmIdx);       // e[4][NH], 1/L[NH]
     constexpr int kSw = NH / 4 < 8 ? NH / 4 : 8;   // chunks per swizzle group (row = NH/4 chunks)
     auto row_chunk = [](int row, int c) { return (c & ~(kSw - 1)) | ((c ^ row) & (kSw - 1)); };
-    cluster_sync_all();   // every CTA is past its main loop
+    // The receive slots overlay Q and the first KV stage, which this CTA's
+    // last GEMM2 may still be reading: retire it before peers may write.
+    if (warp < 4 && n_tiles > 0)
+      mbar_wait_bounded(bar(kBarODone), (n_tiles - 1) & 1, abort_flag, p.timeout_ns);
+    cluster_sync_all();   // every CTA is past its main loop, its UMMAs retired
     if (warp < 4) {
-      if (n_tiles > 0)
-        mbar_wait_bounded(bar(kBarODone), (n_tiles - 1) & 1, abort_flag, p.timeout_ns);
       tc_fence_after();
       if (tid < NH) {
         for (int q = 0; q < nranks; ++q) {
@@ -1110,7 +1145,7 @@ cudaError_t launch_fwd(const Params& p, int splits, cudaStream_t stream) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(p.T) * static_cast<unsigned>(splits), 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.dynamicSmemBytes = Lay<NH>::kSmemBytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -1128,7 +1163,7 @@ template <int NH, bool FP8>
 cudaError_t set_smem_attr() {
   return cudaFuncSetAttribute(sparse_mla_fwd_kernel<NH, FP8>,
                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              static_cast<int>(kSmemBytes));
+                              static_cast<int>(Lay<NH>::kSmemBytes));
 }
 
 int prepare_current_device(int* dev_out) {
