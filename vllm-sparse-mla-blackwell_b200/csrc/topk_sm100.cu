@@ -15,19 +15,23 @@
 //   +NaN above +inf.
 //
 // Design: one CTA of 512 threads per row, radix selection on order-preserving
-// 32-bit keys. The row goes through shared memory in chunks of up to 36K
+// 32-bit keys. The row goes through shared memory in chunks of up to 32K
 // values, each brought in by one bulk copy (plus plain loads for its ragged
 // ends); a row that fits in one chunk is loaded once.
 //   1. Histogram of the top 11 key bits over the row (four copies, so shared
 //      atomics collide across four warps at most); a block-wide suffix scan
-//      finds the bin d0 holding the k-th largest key.
+//      finds the bin d0 holding the k-th largest key. The row passes read
+//      shared memory in 16-byte vectors: in each sweep of 8192 values, warp w
+//      reads the 512 values from 512 w, lane l the words 4 l + 128 q + (0..3)
+//      for q = 0..3, so each warp load covers 512 contiguous bytes and a
+//      thread has its 16 values in flight at once.
 //   2. One pass over the row writes every position whose top bits are above
 //      d0 and gathers the keys in bin d0 (typically a few percent of the row)
-//      with their positions as candidates; each thread counts its strided
-//      share, and a block scan of the counts places every write without
-//      atomics or per-element warp votes.
-//   3. The remaining 21 bits are resolved on the candidates alone (5-, 8- and
-//      8-bit digits, stopping as soon as a whole bin is taken), and the
+//      with their positions as candidates; each thread counts its share, and
+//      a block scan of the counts places every write without atomics or
+//      per-element warp votes.
+//   3. The remaining 21 bits are resolved on the candidates alone (10- and
+//      11-bit digits, stopping as soon as a whole bin is taken), and the
 //      candidates above the threshold plus the first of those equal to it
 //      are written.
 // A row whose bin d0 holds more than kCand keys (heavy ties) resolves the
@@ -47,7 +51,7 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kBins0 = 2048;              // first digit: key bits 31..21
 constexpr int kBins = 256;                // candidate digits: 8 bits
 constexpr int kHists = 4;                 // warp w adds into first-digit histogram w % kHists
-constexpr int kChunk = 36 * 1024;         // keys held in shared memory at a time
+constexpr int kChunk = 32 * 1024;         // keys held in shared memory at a time (4 sweeps)
 constexpr int kCand = 4096;               // candidates (keys in the threshold bin) kept
 constexpr int kMaxTopk = 16384;
 constexpr unsigned kStatusTimeout = 1u;
@@ -247,15 +251,41 @@ __global__ void __launch_bounds__(kThreads, 1) topk_per_row_kernel(const Params 
   uint32_t* const my_hist = whist + (warp % kHists) * kBins0;
   for (int i = tid; i < kHists * kBins0; i += kThreads) whist[i] = 0;
   __syncthreads();
+  // keys[i] is word off + i of the 16-byte aligned keys_raw; a chunk spans
+  // words [off, off + clen)
+  const int off = static_cast<int>((4u - head) & 3u);
+  const int lane = tid & 31;
 #pragma unroll 1
   for (long long c0 = 0; c0 < len; c0 += kChunk) {
     const long long clen = len - c0 < kChunk ? len - c0 : kChunk;
     load_chunk(c0, clen);
-#pragma unroll 4
-    for (long long i = tid; i < clen; i += kThreads) {
-      const uint32_t u = order_key(__uint_as_float(keys[i]));
-      keys[i] = u;
-      atomicAdd(&my_hist[u >> 21], 1u);
+    const int W = off + static_cast<int>(clen);
+#pragma unroll 1
+    for (int s0 = 0; s0 < W; s0 += 16 * kThreads) {
+      const int base = s0 + 512 * warp + 4 * lane;
+      uint4 v[4] = {};
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (base + 128 * q < W) v[q] = *reinterpret_cast<const uint4*>(keys_raw + base + 128 * q);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int a = base + 128 * q;
+        if (a < W) {
+          uint32_t w[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            w[c] = order_key(__uint_as_float(w[c]));
+            if (a + c >= off && a + c < W) atomicAdd(&my_hist[w[c] >> 21], 1u);
+          }
+          if (a >= off && a + 4 <= W) {
+            *reinterpret_cast<uint4*>(keys_raw + a) = make_uint4(w[0], w[1], w[2], w[3]);
+          } else {
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              if (a + c >= off && a + c < W) keys_raw[a + c] = w[c];
+          }
+        }
+      }
     }
     __syncthreads();
   }
@@ -289,32 +319,61 @@ __global__ void __launch_bounds__(kThreads, 1) topk_per_row_kernel(const Params 
       for (long long i = tid; i < clen; i += kThreads) keys[i] = order_key(__uint_as_float(keys[i]));
       __syncthreads();
     }
-    const int n_mine = static_cast<int>((clen - tid + kThreads - 1) / kThreads);
+    const int W = off + static_cast<int>(clen);
     uint32_t ng = 0, ne = 0;
-#pragma unroll 4
-    for (int j = 0; j < n_mine; ++j) {
-      const uint32_t dg = keys[tid + j * kThreads] >> 21;
-      ng += dg > d0;
-      ne += dg == d0;
+#pragma unroll 1
+    for (int s0 = 0; s0 < W; s0 += 16 * kThreads) {
+      const int base = s0 + 512 * warp + 4 * lane;
+      uint4 v[4] = {};
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (base + 128 * q < W) v[q] = *reinterpret_cast<const uint4*>(keys_raw + base + 128 * q);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int a = base + 128 * q;
+        const uint32_t w[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const bool ok = a + c >= off && a + c < W;
+          const uint32_t dg = w[c] >> 21;
+          ng += ok && dg > d0;
+          ne += ok && dg == d0;
+        }
+      }
     }
     uint32_t og, oe, tg, te;
     block_scan2(ng, ne, wcnt, og, oe, tg, te);
     og += gt_base;
     oe += eq_base;
-    for (int j = 0; j < n_mine; ++j) {
-      const long long i = tid + static_cast<long long>(j) * kThreads;
-      const uint32_t u = keys[i];
-      const uint32_t dg = u >> 21;
-      if (dg > d0) {
-        out[og++] = static_cast<int32_t>(c0 + i);
-      } else if (dg == d0) {
-        if (keep) {
-          cand_key[oe] = u;
-          cand_pos[oe] = static_cast<uint32_t>(c0 + i);
-        } else if (c0_count == k_rem) {
-          out[n_gt0 + oe] = static_cast<int32_t>(c0 + i);   // the whole bin is taken
+#pragma unroll 1
+    for (int s0 = 0; s0 < W; s0 += 16 * kThreads) {
+      const int base = s0 + 512 * warp + 4 * lane;
+      uint4 v[4] = {};
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (base + 128 * q < W) v[q] = *reinterpret_cast<const uint4*>(keys_raw + base + 128 * q);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int a = base + 128 * q;
+        const uint32_t w[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          if (a + c < off || a + c >= W) continue;
+          const uint32_t u = w[c];
+          const uint32_t dg = u >> 21;
+          const long long i = a + c - off;
+          if (dg > d0) {
+            out[og++] = static_cast<int32_t>(c0 + i);
+          } else if (dg == d0) {
+            if (keep) {
+              cand_key[oe] = u;
+              cand_pos[oe] = static_cast<uint32_t>(c0 + i);
+            } else if (c0_count == k_rem) {
+              out[n_gt0 + oe] = static_cast<int32_t>(c0 + i);   // the whole bin is taken
+            }
+            ++oe;
+          }
         }
-        ++oe;
       }
     }
     gt_base += tg;
@@ -326,28 +385,37 @@ __global__ void __launch_bounds__(kThreads, 1) topk_per_row_kernel(const Params 
   // ---- the k_rem largest of the threshold bin's keys (bits 20..0 still open)
   int32_t* const out_c = out + n_gt0;
   if (keep) {
-    // candidates in shared memory: 8-bit digits over bits 20..0 (13/8 split:
-    // a 5-bit digit first, then two 8-bit digits)
+    // candidates in shared memory: two digits over bits 20..0 (bits 20..11
+    // in 1024 bins, then 10..0 in 2048), each with its own histogram (the
+    // merged first-digit histogram and the first per-warp copy, both free
+    // now), zeroed together up front. ctl and wsum are rewritten only after
+    // the next pass's first barrier, which every thread reaches after
+    // reading them, so a pass needs no closing barrier.
     uint32_t prefix = d0 << 21, mask = 0xFFE00000u;
-    const int shifts[3] = {16, 8, 0};
-    const uint32_t widths[3] = {0x1Fu, 0xFFu, 0xFFu};
     bool settled = c0_count == k_rem;
     const int n = static_cast<int>(c0_count);
-#pragma unroll 1
-    for (int pss = 0; pss < 3 && !settled; ++pss) {
-      for (int i = tid; i < kBins; i += kThreads) hist[i] = 0;
-      __syncthreads();
-      for (int i = tid; i < n; i += kThreads) {
-        const uint32_t u = cand_key[i];
-        if ((u & mask) == prefix) atomicAdd(&hist[(u >> shifts[pss]) & widths[pss]], 1u);
+    if (!settled) {
+      for (int i = tid; i < kBins0; i += kThreads) {
+        hist[i] = 0;
+        whist[i] = 0;
       }
       __syncthreads();
-      find_digit(hist, kBins, k_rem, wsum, ctl);
-      prefix |= ctl[0] << shifts[pss];
-      mask |= widths[pss] << shifts[pss];
+    }
+#pragma unroll 1
+    for (int pss = 0; pss < 2 && !settled; ++pss) {
+      const int shift = pss == 0 ? 11 : 0;
+      const uint32_t width = pss == 0 ? 0x3FFu : 0x7FFu;
+      uint32_t* const h = pss == 0 ? hist : whist;
+      for (int i = tid; i < n; i += kThreads) {
+        const uint32_t u = cand_key[i];
+        if ((u & mask) == prefix) atomicAdd(&h[(u >> shift) & width], 1u);
+      }
+      __syncthreads();
+      find_digit(h, static_cast<int>(width) + 1, k_rem, wsum, ctl);
+      prefix |= ctl[0] << shift;
+      mask |= width << shift;
       k_rem -= ctl[1];
       settled = ctl[2] == k_rem;
-      __syncthreads();
     }
     // candidates above the prefix, then the first k_rem equal to it: per-thread
     // counts over a strided share of the candidates and a block scan
