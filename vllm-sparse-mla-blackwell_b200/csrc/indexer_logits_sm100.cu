@@ -47,6 +47,7 @@
 #include <cmath>
 #include <cstdint>
 #include <mutex>
+#include <utility>
 
 #include "glm53_sparse_mla.h"
 #include "sm100_ptx.cuh"
@@ -162,6 +163,11 @@ __global__ void __launch_bounds__(kThreads, 1) indexer_logits_kernel(const __gri
                                   ? p0 + kTile * kTilesPerCta
                                   : static_cast<long long>(p.max_model_len);
   const long long row0 = static_cast<long long>(b) * NEXT_N;
+  // Programmatic dependent launch: the logits and the inputs may come from
+  // the previous kernel in the stream. Dependents may launch at once: they
+  // wait in turn for this grid to finish.
+  griddep_wait();
+  griddep_launch_dependents();
   // visible length of each of the request's tokens, and the longest
   long long lens[NEXT_N];
   long long ctx = 0;
@@ -387,6 +393,25 @@ EncodeTiledFn encoder() {
 // 3-D view of the cache values: 128 bytes x block_size rows x num_blocks,
 // boxes of min(block_size, 128) rows of one block, 128-byte swizzle (the
 // layout the UMMA descriptors read).
+// Launch with programmatic stream serialization, so this grid may begin
+// launching while the previous kernel in the stream drains; the kernel's
+// griddepcontrol.wait, before its first global access, keeps the order.
+template <typename... Params, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 bool make_kv_map(CUtensorMap* map, const Params& p) {
   EncodeTiledFn enc = encoder();
   if (enc == nullptr) return false;
@@ -415,8 +440,8 @@ cudaError_t launch(const Params& p, const CUtensorMap& map, int B, cudaStream_t 
   }
   const dim3 grid(static_cast<unsigned>((p.max_model_len + kTile * kTilesPerCta - 1) / (kTile * kTilesPerCta)),
                   static_cast<unsigned>(B));
-  indexer_logits_kernel<H, NEXT_N><<<grid, kThreads, Layout<H * NEXT_N>::kBytes, stream>>>(p, map);
-  return cudaGetLastError();
+  return launch_pdl(indexer_logits_kernel<H, NEXT_N>, grid, dim3(kThreads), Layout<H * NEXT_N>::kBytes,
+                    stream, p, map);
 }
 
 bool aligned(const void* ptr, uintptr_t a) { return (reinterpret_cast<uintptr_t>(ptr) & (a - 1)) == 0; }

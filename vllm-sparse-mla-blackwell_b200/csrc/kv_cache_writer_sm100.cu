@@ -97,6 +97,11 @@ __device__ __forceinline__ uint2 quantize8(const uint4 w, const float s, const f
 
 template <bool kFp8>
 __global__ void __launch_bounds__(32 * kWarpsPerBlock) concat_and_cache_kernel(const Params p) {
+  // Programmatic dependent launch: the new rows come from the previous
+  // kernel in the stream, so wait for it before any global access;
+  // dependents may launch at once (they wait in turn for this grid).
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const long long t = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + (threadIdx.x >> 5);
   if (t >= p.T) return;
   const int lane = threadIdx.x & 31;
@@ -168,12 +173,20 @@ extern "C" int glm53_concat_and_cache(const void* kv_c, int64_t kv_c_stride, int
   p.scale = scale;
   const long long blocks = (T + kWarpsPerBlock - 1) / kWarpsPerBlock;
   if (blocks > 0x7FFFFFFFll) return GLM53_ERR_RANK;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (fp8)
-    concat_and_cache_kernel<true><<<static_cast<unsigned>(blocks), 32 * kWarpsPerBlock, 0, s>>>(p);
-  else
-    concat_and_cache_kernel<false><<<static_cast<unsigned>(blocks), 32 * kWarpsPerBlock, 0, s>>>(p);
-  return cudaGetLastError() == cudaSuccess ? GLM53_OK : GLM53_ERR_CUDA;
+  // launched with programmatic stream serialization, so the grid may begin
+  // launching while the previous kernel in the stream drains
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks));
+  cfg.blockDim = dim3(32 * kWarpsPerBlock);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = fp8 ? cudaLaunchKernelEx(&cfg, concat_and_cache_kernel<true>, p)
+                            : cudaLaunchKernelEx(&cfg, concat_and_cache_kernel<false>, p);
+  return e == cudaSuccess ? GLM53_OK : GLM53_ERR_CUDA;
 }
 
 extern "C" int glm53_concat_and_cache_status(uint32_t* status, int clear) {

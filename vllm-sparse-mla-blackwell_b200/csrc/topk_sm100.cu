@@ -40,6 +40,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <utility>
 
 #include "glm53_sparse_mla.h"
 
@@ -164,6 +165,11 @@ __device__ __forceinline__ void block_scan2(uint32_t a, uint32_t b, uint32_t* sc
 }
 
 __global__ void __launch_bounds__(kThreads, 1) topk_per_row_kernel(const Params p) {
+  // Programmatic dependent launch: the logits come from the previous kernel
+  // in the stream, so wait for it before any global access; dependents may
+  // launch at once (they wait in turn for this grid to finish).
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   extern __shared__ __align__(16) uint32_t smem[];
   uint32_t* const keys_raw = smem;                               // [kChunk + 4]
   uint32_t* const whist = smem + kChunk + 4;                     // [kHists][kBins0]
@@ -509,6 +515,25 @@ __global__ void __launch_bounds__(kThreads, 1) topk_per_row_kernel(const Params 
   }
 }
 
+// Launch with programmatic stream serialization, so this grid may begin
+// launching while the previous kernel in the stream drains; the kernel's
+// griddepcontrol.wait, before its first global access, keeps the order.
+template <typename... Params, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 bool g_attr_set[64] = {};
 
 }  // namespace topk
@@ -558,9 +583,10 @@ extern "C" int glm53_topk_per_row(const float* logits, int64_t num_rows, int64_t
   p.out_stride = out_stride;
   p.k = topk;
   p.timeout_ns = 1000000000ull;
-  topk_per_row_kernel<<<static_cast<unsigned>(num_rows), kThreads, kSmemBytes,
-                        static_cast<cudaStream_t>(stream)>>>(p);
-  return cudaGetLastError() == cudaSuccess ? GLM53_OK : GLM53_ERR_CUDA;
+  return launch_pdl(topk_per_row_kernel, dim3(static_cast<unsigned>(num_rows)), dim3(kThreads),
+                    kSmemBytes, static_cast<cudaStream_t>(stream), p) == cudaSuccess
+             ? GLM53_OK
+             : GLM53_ERR_CUDA;
 }
 
 extern "C" int glm53_topk_status(uint32_t* status, int clear) {
