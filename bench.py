@@ -729,6 +729,7 @@ def run_topk_reference(args, dist: Dist):
     cpu = topk_cpu(sets[0].numpy(), args.ctx, max(1.0, min(args.cpu_seconds, 30.0)))
     line = {"impl": "reference", "metric": f"indexer top-{TOPK_K} {TK_UNIT} (decode, ctx {args.ctx})",
             "value": cpu["value"], "unit": TK_UNIT, "n_gpus": dist.world, "steps": args.steps,
+            "ms_per_step": round(args.rows / cpu["value"] * 1e3, 5),
             "warmup": max(args.warmup, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
             "config": topk_desc(args), "cpu_baseline": cpu,
@@ -885,6 +886,7 @@ def run_indexer_reference(args, dist: Dist):
     line = {"impl": "reference",
             "metric": f"indexer logits {IX_UNIT} (decode, ctx {args.ctx}, {IDX_HEADS} heads)",
             "value": cpu["value"], "unit": IX_UNIT, "n_gpus": dist.world, "steps": args.steps,
+            "ms_per_step": round(args.rows / cpu["value"] * 1e3, 5),
             "warmup": max(args.warmup, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
             "config": indexer_desc(args), "cpu_baseline": cpu,
@@ -1120,6 +1122,7 @@ def run_cache_write_reference(args, dist: Dist):
     cpu = cache_write_cpu(sets[0], fp8, max(1.0, min(args.cpu_seconds, 30.0)))
     line = {"impl": "reference", "metric": f"latent KV-cache writes ({args.kv}), {CW_UNIT}",
             "value": cpu["value"], "unit": CW_UNIT, "n_gpus": dist.world, "steps": args.steps,
+            "ms_per_step": round(args.tokens / cpu["value"] * 1e3, 5),
             "warmup": max(args.warmup, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
             "config": cache_write_desc(args, fp8), "cpu_baseline": cpu,
