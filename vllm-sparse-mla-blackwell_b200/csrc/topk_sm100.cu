@@ -126,6 +126,48 @@ __device__ __forceinline__ void find_digit(const uint32_t* hist, int nb, uint32_
   __syncthreads();
 }
 
+// find_digit over the first digit, reading the kHists per-warp histogram
+// copies directly: thread t sums bins 4t..4t+3 of every copy (one 16-byte
+// load per copy), which saves a merge pass and its barrier.
+__device__ __forceinline__ void find_digit0(const uint32_t* whist, uint32_t need, uint32_t* wsum,
+                                            uint32_t* ctl) {
+  static_assert(kBins0 == 4 * kThreads, "four first-digit bins per thread");
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  uint32_t c[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+  for (int w = 0; w < kHists; ++w) {
+    const uint4 v = *reinterpret_cast<const uint4*>(whist + w * kBins0 + 4 * tid);
+    c[0] += v.x;
+    c[1] += v.y;
+    c[2] += v.z;
+    c[3] += v.w;
+  }
+  const uint32_t s = c[0] + c[1] + c[2] + c[3];
+  uint32_t incl = s;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const uint32_t v = __shfl_down_sync(0xFFFFFFFFu, incl, off);
+    if (lane + off < 32) incl += v;
+  }
+  if (lane == 0) wsum[warp] = incl;
+  __syncthreads();
+  for (int w = warp + 1; w < kWarps; ++w) incl += wsum[w];
+  uint32_t above = incl - s;
+  if (above < need && need <= incl) {
+#pragma unroll
+    for (int j = 3; j >= 0; --j) {
+      if (above + c[j] >= need) {
+        ctl[0] = static_cast<uint32_t>(4 * tid + j);
+        ctl[1] = above;
+        ctl[2] = c[j];
+        break;
+      }
+      above += c[j];
+    }
+  }
+  __syncthreads();
+}
+
 // Block-wide exclusive prefix sums of two per-thread counts (thread order):
 // returns this thread's offsets and the block totals. Uses scratch[2 * kWarps].
 __device__ __forceinline__ void block_scan2(uint32_t a, uint32_t b, uint32_t* scratch,
@@ -295,14 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_per_row_kernel(const Params 
     }
     __syncthreads();
   }
-  for (int b = tid; b < kBins0; b += kThreads) {
-    uint32_t c = 0;
-#pragma unroll
-    for (int w = 0; w < kHists; ++w) c += whist[w * kBins0 + b];
-    hist[b] = c;
-  }
-  __syncthreads();
-  find_digit(hist, kBins0, static_cast<uint32_t>(k), wsum, ctl);
+  find_digit0(whist, static_cast<uint32_t>(k), wsum, ctl);
   const uint32_t d0 = ctl[0];
   uint32_t k_rem = static_cast<uint32_t>(k) - ctl[1];
   const uint32_t c0_count = ctl[2];
