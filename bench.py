@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Benchmark: sparse-MLA query-tokens/s at 64 heads, top-k 2048 (BASELINE C2).
+"""Benchmark: sparse-MLA query-tokens/s at 64 heads, top-k 2048 (C2 decode batch).
 
 One step = one launch of the sparse-MLA op over one decode batch: 32 query
 tokens x 64 heads, top-k 2048 over a 131072-slot paged bf16 KV pool (block 64,
@@ -162,6 +162,21 @@ def make_workload(args, W, seed: int, device, heads: int, head_offset: int = 0):
     if heads and heads != w.H:
         w.q = w.q[:, head_offset:head_offset + heads].contiguous()
     return w
+
+
+def attention_config(args, w, heads_total: int, world: int) -> dict:
+    """The `config` object of the attention arms; the reference arm prints the
+    same one, computed from the arguments and the workload's shapes only."""
+    cfg = workload_desc(args, w, heads_total)
+    n_sets = max(1, args.sets)
+    pool_gb = n_sets * w.kv.numel() * w.kv.element_size() / 1e9
+    cfg.update({"parallelism": (f"dp{world}" if args.shard == "tokens" else f"tp{world}-heads"),
+                "l2": f"{n_sets} rotating input sets, {pool_gb:.2f} GB of KV pools "
+                      "(>> 126 MB L2); consecutive steps share no memory",
+                "timing": "K steps in one CUDA graph, CUDA events, max over ranks",
+                "splits": args.splits or "auto",
+                "allgather": bool(args.allgather and world > 1 and args.shard == "heads")})
+    return cfg
 
 
 def workload_desc(args, w, heads_total: int) -> dict:
@@ -395,15 +410,7 @@ def run_ours(args, dist: Dist):
         cpu = cpu_baseline(w0, args.cpu_seconds)
 
     if dist.rank == 0:
-        cfg = workload_desc(args, w0, heads_total)
-        cfg.update({"parallelism": (f"dp{dist.world}" if args.shard == "tokens"
-                                    else f"tp{dist.world}-heads"),
-                    "l2": f"{len(sets)} rotating input sets, "
-                          f"{sum(w.kv.numel() * w.kv.element_size() for w in sets) / 1e9:.2f} GB "
-                          "of KV pools (>> 126 MB L2); consecutive steps share no memory",
-                    "timing": "K steps in one CUDA graph, CUDA events, max over ranks",
-                    "splits": int(os.environ.get("GLM53_SPLITS", "0")) or "auto",
-                    "allgather": bool(gathered is not None)})
+        cfg = attention_config(args, w0, heads_total, dist.world)
         line = {"metric": METRIC if args.workload == "c2" else f"sparse-MLA {UNIT} ({args.workload})",
                 "value": round(value, 1), "unit": UNIT, "n_gpus": dist.world, "steps": args.steps,
                 "warmup": max(args.warmup, 3), "ms_per_step": round(ms_step, 5),
@@ -1021,8 +1028,9 @@ def run_e2e(args, G, sets, device, dist: Dist):
                     f"overlapped across {n} streams"}
 
 
-def _oracle_inputs(w):
-    from glm53_sparse_mla import workloads as W
+def _oracle_inputs(w, W=None):
+    if W is None:
+        from glm53_sparse_mla import workloads as W
     kv = W.dequantize_fp8(w.kv, w.kv_scale) if w.kv.dtype == torch.float8_e4m3fn else w.kv
     return (w.q.float().cpu().numpy(), kv.float().cpu().numpy(), w.indices.cpu().numpy())
 
@@ -1056,9 +1064,24 @@ def cpu_baseline(w, seconds: float, heads: int | None = None):
                       f"{dt:.1f} s"}
 
 
+def _workloads_standalone():
+    """workloads.py loaded by file path, without importing the package: the
+    package import loads the CUDA extension, which the reference arm must not
+    map."""
+    import importlib.util
+    path = os.path.join(REPO, "vllm-sparse-mla-blackwell_b200", "glm53_sparse_mla", "workloads.py")
+    spec = importlib.util.spec_from_file_location("_glm53_workloads_standalone", path)
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[spec.name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
 def run_reference(args, dist: Dist):
     """Reference arm: the reference's CPU implementation of the path (the
-    oracle port) on the host cores, rank 0 only; other ranks exit at once."""
+    oracle port) on the host cores, rank 0 only; other ranks exit at once.
+    Inputs are generated on the host and nothing of this repository's CUDA
+    extension is loaded."""
     if dist.rank != 0:
         return
     # torchrun pins OMP threads to 1 per rank; the CPU arm uses every core
@@ -1067,11 +1090,10 @@ def run_reference(args, dist: Dist):
         threadpool_limits(limits=os.cpu_count() or 1)
     except Exception:  # pragma: no cover
         pass
-    from glm53_sparse_mla import workloads as W
-    device = "cuda" if torch.cuda.is_available() else "cpu"
-    w = make_workload(args, W, 100, device, 0)
+    W = _workloads_standalone()
+    w = make_workload(args, W, 100, "cpu", 0)
     from oracle import sparse_mla_oracle as O
-    q, kv, idx = _oracle_inputs(w)
+    q, kv, idx = _oracle_inputs(w, W)
     # size each step (one query token; a head slice of it if K is large) so
     # the whole run stays within about three minutes
     t0 = time.perf_counter()
@@ -1098,13 +1120,17 @@ def run_reference(args, dist: Dist):
         cores = os.cpu_count() or 1
     sample = (f"one query token per step ({heads} of {w.H} heads, scaled), numpy fp32 oracle "
               "restating the reference's tests/reference.py")
+    heads_total = 64 if args.workload in ("c2", "c5") else (32 if args.workload == "c3" else 16)
+    if args.heads:
+        heads_total = args.heads
     line = {"impl": "reference", "metric": METRIC if args.workload == "c2" else
             f"sparse-MLA {UNIT} ({args.workload})", "value": round(value, 3), "unit": UNIT,
             "n_gpus": dist.world, "steps": args.steps, "warmup": max(args.warmup, 3),
             "ms_per_step": round(dt / args.steps * 1e3, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "scaling": "weak" if args.shard == "tokens" else "strong",
+            "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded, random init)",
-            "config": workload_desc(args, w, w.H),
+            "config": attention_config(args, w, heads_total, dist.world),
             "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": int(cores),
                              "kind": "port", "sample": sample},
             "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,

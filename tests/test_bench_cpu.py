@@ -1,6 +1,6 @@
 """bench.py's reference arm, which runs on the host cores: the one-line JSON
-contract the round-end driver reads (one line on stdout, the keys it reads,
-the reference-arm fields), without a GPU.
+contract a benchmark harness reads (one line on stdout, its keys, the
+reference-arm fields), without a GPU.
 
 The reference arm times the numpy oracle (the CPU restatement of the
 reference's path) on a bounded sample of the C2 workload.
@@ -47,3 +47,34 @@ def test_reference_arm_prints_one_contract_line(op):
     e2e = d["e2e"]
     assert e2e["value"] == d["value"] and e2e["unit"] == d["unit"]
     assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
+
+
+_MAPPED = r"""
+import runpy, sys
+sys.argv = ["bench.py", "--impl", "reference", "--steps", "2", "--warmup", "3"]
+runpy.run_path("bench.py", run_name="__main__")
+maps = open("/proc/self/maps").read()
+libs = sorted({ln.split()[-1] for ln in maps.splitlines() if "glm53" in ln})
+print("MAPPED " + ";".join(libs) + " PKG " + str("glm53_sparse_mla" in sys.modules))
+"""
+
+
+def test_reference_arm_maps_no_repo_library_and_keeps_the_config():
+    """The attention reference arm times the CPU restatement only: it maps no
+    shared library of this repository (the package import would load the CUDA
+    extension), and its config carries the keys the repository's arm prints
+    for the same arguments."""
+    res = subprocess.run([sys.executable, "-c", _MAPPED], capture_output=True, text=True,
+                         timeout=600, cwd=REPO)
+    assert res.returncode == 0, res.stderr[-2000:]
+    lines = [ln for ln in res.stdout.splitlines() if ln.strip()]
+    line = json.loads(lines[0])
+    tail = lines[-1]
+    assert tail.startswith("MAPPED "), tail
+    libs, pkg = tail[len("MAPPED "):].split(" PKG ")
+    assert libs == "", libs
+    assert pkg == "False"
+    cfg = line["config"]
+    for key in ("workload", "parallelism", "l2", "timing", "splits", "allgather"):
+        assert key in cfg, key
+    assert cfg["parallelism"] == "dp1" and cfg["splits"] == "auto" and cfg["allgather"] is False
