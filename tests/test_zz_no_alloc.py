@@ -7,7 +7,7 @@ scratch is a 32 MiB array built into the library. These tests call it
 through the C ABI and compare it with glm53_sparse_mla_fwd on the same
 inputs, within the parity tolerance used everywhere else, on two calls in a
 row (the scratch keeps the first call's contents when the second one runs),
-and check that a shape needing more scratch than the array holds is refused
+and with the CPU oracle directly, and check that a shape needing more scratch than the array holds is refused
 before any launch.
 
 The file name makes pytest collect it last.
@@ -21,6 +21,7 @@ import pytest
 import torch
 
 from conftest import COS_TOL, REL_TOL, parity_metrics
+from test_parity_gpu import _check, _oracle
 
 pytestmark = pytest.mark.gpu
 
@@ -67,6 +68,10 @@ def test_noalloc_matches_fwd_on_two_calls_in_a_row():
         torch.cuda.synchronize()
         assert rc_ref == 0 and rc == 0, (rc_ref, rc)
         _same(got, ref, f"{w.name}/splits={splits}")
+        # and against the CPU oracle directly, on the second call too, when
+        # the scratch still holds the first call's partials
+        oref, _ = _oracle(w)
+        _check(f"{w.name}/noalloc/splits={splits}", got, oref, w.indices)
         fin = torch.isfinite(ref_lse)
         assert torch.equal(fin, torch.isfinite(lse))
         assert (lse[fin] - ref_lse[fin]).abs().max().item() <= 1e-3
