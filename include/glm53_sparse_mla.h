@@ -192,17 +192,38 @@ int glm53_sparse_mla_prepare(void);
  */
 int glm53_sparse_mla_device_status(uint32_t* status, int clear);
 
+/*
+ * Set the wall-time limit of every pipeline wait inside the attention kernel
+ * for launches made from now on (a CUDA graph keeps the limit it was
+ * captured with). ns == 0 restores the default: GLM53_WAIT_TIMEOUT_MS
+ * milliseconds if that environment variable is set, else 1 s. When a wait
+ * runs out, its CTA stops waiting, retires its own tensor-core work, releases
+ * its tensor memory and raises GLM53_DEV_TIMEOUT; the output of that launch
+ * is undefined. Process-wide; safe to call from any thread.
+ * No counterpart in the reference, whose waits are __syncthreads and a
+ * launch check (csrc/sparse_mla.cu:440-452); the bound is how a pipeline
+ * fault becomes an error status here instead of a hung GPU.
+ */
+int glm53_sparse_mla_set_wait_timeout_ns(uint64_t ns);
+
 /* Human-readable text for a glm53_status code. */
 const char* glm53_sparse_mla_strerror(int code);
 
 /*
- * Gather-only bandwidth probe: copies the rows named by `indices` ([T, topk],
- * < 0 skipped) of a bf16 [R, 512] pool into shared memory and discards them.
- * Measures the achievable indexed-gather rate that bounds the attention
- * kernel. Replaces the bench-only probe bench/gather_roof.cu:13-55.
+ * Gather-only bandwidth probe: the attention kernel's gather (16-byte
+ * cp.async per lane into 64-row swizzled shared-memory tiles, 1 KiB bf16
+ * rows) with no math, over a 3-stage ring of 64 KiB tiles. The flattened
+ * [T, topk] index list is cut into `ctas` equal contiguous ranges, one per
+ * CTA (ctas == 0: one CTA per token, the reference probe's grid); entries
+ * outside [0, kv_rows) are skipped. sink (NULL, or one uint32 per CTA)
+ * receives the XOR of the first 32-bit word of every row the CTA gathered.
+ * The time of one call bounds how fast any kernel can gather the same rows
+ * with this load scheme: the attention's gather roof.
+ * Replaces the bench-only probe gather_only / gather_roof of the reference
+ * (bench/gather_roof.cu:13-55, driven by bench/gather_roof.py:12-23).
  */
 int glm53_gather_roof(const void* kv, const int32_t* indices, int64_t T, int64_t topk,
-                      int64_t kv_rows, void* sink, void* stream);
+                      int64_t kv_rows, int ctas, uint32_t* sink, void* stream);
 
 /*
  * Latent KV-cache writer (the write that feeds the attention above).

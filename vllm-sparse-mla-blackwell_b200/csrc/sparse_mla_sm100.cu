@@ -55,11 +55,15 @@
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdint>
 #include <cstdlib>
 #include <mutex>
 #include <type_traits>
+
+#include <nvtx3/nvToolsExt.h>
 
 #include "glm53_sparse_mla.h"
 #include "sm100_ptx.cuh"
@@ -99,7 +103,7 @@ struct Lay {
   static constexpr uint32_t kSmIdx = kSmP + 2 * kPBytes;           // int32[kMaxChunk]
   static constexpr uint32_t kSmHead = kSmIdx + 4 * kMaxChunk;      // m[64] l[64] alpha[64] f[64]
   static constexpr uint32_t kSmBar = kSmHead + 4 * 64 * 4;         // mbarriers
-  static constexpr uint32_t kSmMisc = kSmBar + 16 * 8;             // tmem base, counts, abort flag
+  static constexpr uint32_t kSmMisc = kSmBar + 24 * 8;             // tmem base, counts, abort flag
   static constexpr uint32_t kSmMlRecv = kSmMisc + 64;              // m[8][64], l[8][64] of the peers
   static constexpr uint32_t kSmUsed = kSmMlRecv + 2 * 8 * 64 * 4;
   static constexpr uint32_t kSmemBytes = kSmUsed + 1024;           // + slack to align the base
@@ -117,8 +121,15 @@ enum : int {
   kBarDrain = 11,    // GEMM1 issuer's UMMAs all retired
   kBarQFull = 12,    // all threads (cp.async) -> GEMM1 issuer: Q landed
   kBarKvFirst = 13,  // [2] all threads -> GEMM1 issuer: tile 0 / 1 loaded
-  kNumBars = 15
+  kBarG2Drain = 15,  // [4] GEMM2 issuer of softmax warp w: its UMMAs all retired
+  kNumBars = 19
 };
+
+// Bound of the waits that drain this CTA's own UMMAs before TMEM is released.
+// UMMAs wait on nothing once issued, so these complete in microseconds; the
+// bound is fixed (not the configurable pipeline-wait limit) so that a short
+// pipeline limit can never release TMEM under a UMMA still in flight.
+constexpr unsigned long long kDrainTimeoutNs = 1000000000ull;
 
 // misc words
 enum : int { kMiscTmem = 0, kMiscWarpCount = 2, kMiscAbort = 10 };
@@ -243,6 +254,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
     mbar_init(bar(kBarQFull), kThreads);
     mbar_init(bar(kBarKvFirst), kThreads);
     mbar_init(bar(kBarKvFirst + 1), kThreads);
+    for (int w = 0; w < 4; ++w) mbar_init(bar(kBarG2Drain + w), 1);
     misc[kMiscAbort] = 0;
     fence_mbarrier_init();
   }
@@ -582,7 +594,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
       // Drain: never release TMEM while a UMMA may still write it.
       umma_commit(bar(kBarDrain));
       int no_abort = 0;
-      mbar_wait_bounded(bar(kBarDrain), 0, &no_abort, p.timeout_ns);
+      mbar_wait_bounded(bar(kBarDrain), 0, &no_abort, kDrainTimeoutNs);
     }
     __syncwarp();
   } else if (warp < 4) {
@@ -684,6 +696,15 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
       __syncwarp();
     }
 
+    // Each GEMM2 issuer retires its own UMMAs before anything may release
+    // TMEM. The merge's waits on kBarODone cover this when no wait timed out;
+    // after a timeout they return at once, and this drain is what keeps TMEM
+    // allocated until the last GEMM2 has written it.
+    if (lane == 0 && n_tiles > 0) {
+      umma_commit(bar(kBarG2Drain + warp));
+      int no_abort = 0;
+      mbar_wait_bounded(bar(kBarG2Drain + warp), 0, &no_abort, kDrainTimeoutNs);
+    }
     // publish this CTA's per-head max and sum for the merge
     __syncwarp();
     const float l_tot = l_part + __shfl_xor_sync(0xFFFFFFFFu, l_part, 16);
@@ -1092,25 +1113,50 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
 }
 
 // ---------------------------------------------------------------------------
-// gather-only probe: same access pattern as the attention gather, no math
+// gather-only probe: the attention's gather (16-byte cp.async per lane into
+// the same swizzled 64-row tiles) with no math, over a 3-stage ring
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_2() { asm volatile("cp.async.wait_group 2;" ::: "memory"); }
 
-__global__ void __launch_bounds__(256, 1) gather_roof_kernel(const uint8_t* __restrict__ kv,
-                                                             const int32_t* __restrict__ idx,
-                                                             int topk, long long kv_rows,
-                                                             uint32_t* sink) {
+constexpr int kRoofStages = 3;
+constexpr int kRoofThreads = 256;
+
+// CTA c gathers entries [c * per_cta, min(total, (c + 1) * per_cta)) of the
+// flattened [T, topk] index list; entries outside [0, kv_rows) are skipped.
+// sink[c] = XOR of the first 32-bit word of every row it gathered, so the
+// copies cannot be elided and the result can be checked on the host.
+__global__ void __launch_bounds__(kRoofThreads, 1) gather_roof_kernel(const uint8_t* __restrict__ kv,
+                                                                      const int32_t* __restrict__ idx,
+                                                                      long long total, long long per_cta,
+                                                                      long long kv_rows,
+                                                                      uint32_t* __restrict__ sink) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t sb = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  uint8_t* const gb = smem_raw + (sb - smem_u32(smem_raw));
+  __shared__ uint32_t red[kRoofThreads / 32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int32_t* irow = idx + static_cast<size_t>(blockIdx.x) * topk;
-  const int ntiles = (topk + kRows - 1) / kRows;
+  const long long k0 = static_cast<long long>(blockIdx.x) * per_cta;
+  const long long n = max(0ll, min(per_cta, total - k0));
+  const int ntiles = static_cast<int>((n + kRows - 1) / kRows);
+  uint32_t x = 0;
+  // thread r < 64 folds in row r of a tile that has landed
+  auto check = [&](int t) {
+    if (threadIdx.x < kRows) {
+      const long long k = static_cast<long long>(kRows) * t + threadIdx.x;
+      const int32_t v = k < n ? idx[k0 + k] : -1;
+      if (v >= 0 && v < kv_rows)
+        x ^= *reinterpret_cast<const uint32_t*>(gb + (t % kRoofStages) * kStageBytes + swz(threadIdx.x, 0));
+    }
+  };
   for (int t = 0; t < ntiles; ++t) {
-    const uint32_t stage = sb + (t & 1) * kStageBytes;
-    for (int r = warp; r < kRows; r += 8) {
-      const int k = kRows * t + r;
-      const int32_t v = k < topk ? irow[k] : -1;
+    // stage t % 3 was last read by check(t - 3), before the barrier of the
+    // previous iteration; this barrier orders that read before the overwrite
+    if (t >= kRoofStages) __syncthreads();
+    const uint32_t stage = sb + (t % kRoofStages) * kStageBytes;
+    for (int r = warp; r < kRows; r += kRoofThreads / 32) {
+      const long long k = static_cast<long long>(kRows) * t + r;
+      const int32_t v = k < n ? idx[k0 + k] : -1;
       const bool valid = v >= 0 && v < kv_rows;
       const uint8_t* src = kv + (valid ? static_cast<long long>(v) : 0) * (kDim * 2);
 #pragma unroll
@@ -1120,13 +1166,24 @@ __global__ void __launch_bounds__(256, 1) gather_roof_kernel(const uint8_t* __re
       }
     }
     cp_async_commit();
-    cp_async_wait_1();
+    if (t >= kRoofStages - 1) {
+      cp_async_wait_2();     // tile t - 2 landed (this thread's part)
+      __syncthreads();       // ... and every thread's
+      check(t - (kRoofStages - 1));
+    }
   }
   cp_async_wait_all();
   __syncthreads();
-  uint32_t x;
-  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(x) : "r"(sb + threadIdx.x * 4));
-  if (x == 0x9E3779B9u && sink != nullptr) sink[0] = x;   // keep the copies observable
+  for (int t = max(0, ntiles - (kRoofStages - 1)); t < ntiles; ++t) check(t);
+#pragma unroll
+  for (int k = 16; k >= 1; k >>= 1) x ^= __shfl_xor_sync(0xFFFFFFFFu, x, k);
+  if (lane == 0) red[warp] = x;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t y = 0;
+    for (int w = 0; w < kRoofThreads / 32; ++w) y ^= red[w];
+    if (sink != nullptr) sink[blockIdx.x] = y;
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -1137,7 +1194,16 @@ std::mutex g_mutex;
 bool g_prepared[kMaxDevices] = {};
 int g_sm_count[kMaxDevices] = {};
 int g_cc_major[kMaxDevices] = {};
-unsigned long long g_timeout_ns = 0;
+// Pipeline-wait limit passed to every launch (0: not yet resolved). Set from
+// GLM53_WAIT_TIMEOUT_MS (default 1000 ms) on first use, or by
+// glm53_sparse_mla_set_wait_timeout_ns.
+std::atomic<unsigned long long> g_timeout_ns{0};
+
+unsigned long long default_timeout_ns() {
+  const char* env = std::getenv("GLM53_WAIT_TIMEOUT_MS");
+  const long long ms = env ? std::atoll(env) : 0;
+  return static_cast<unsigned long long>(ms > 0 ? ms : 1000) * 1000000ull;
+}
 int g_env_splits = -1;   // GLM53_SPLITS: forced split count for splits == 0 (-1: unread)
 
 template <int NH, bool FP8>
@@ -1178,11 +1244,7 @@ int prepare_current_device(int* dev_out) {
     const int v = env ? std::atoi(env) : 0;
     g_env_splits = (v == 1 || v == 2 || v == 4 || v == 8) ? v : 0;
   }
-  if (g_timeout_ns == 0) {
-    const char* env = std::getenv("GLM53_WAIT_TIMEOUT_MS");
-    const long long ms = env ? std::atoll(env) : 0;
-    g_timeout_ns = static_cast<unsigned long long>(ms > 0 ? ms : 1000) * 1000000ull;
-  }
+  if (g_timeout_ns.load() == 0) g_timeout_ns.store(default_timeout_ns());
   int major = 0, sms = 0;
   if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
@@ -1199,7 +1261,7 @@ int prepare_current_device(int* dev_out) {
   if (e == cudaSuccess) e = set_smem_attr<64, true>();
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(gather_roof_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(2 * kStageBytes + 1024));
+                             static_cast<int>(kRoofStages * kStageBytes + 1024));
   if (e != cudaSuccess) return GLM53_ERR_CUDA;
   g_prepared[dev] = true;
   return GLM53_OK;
@@ -1299,6 +1361,11 @@ int launch_forward(const void* q, const void* kv, const int32_t* indices, void* 
                    int64_t topk, int kv_dtype, float sm_scale, float kv_scale, int splits,
                    bool use_ws, void* ws, uint64_t ws_bytes, void* stream,
                    const Paged* pg = nullptr) {
+  // A named host range for profilers and tracers (a no-op without one).
+  struct NvtxRange {
+    NvtxRange() { nvtxRangePushA("glm53_sparse_mla_fwd"); }
+    ~NvtxRange() { nvtxRangePop(); }
+  } nvtx_range;
   int rc = glm53_sparse_mla_check(T, H, head_dim, kv_rows, kv_width, topk, kv_dtype, splits);
   if (rc != GLM53_OK) return rc;
   if (T == 0) return GLM53_OK;
@@ -1350,7 +1417,7 @@ int launch_forward(const void* q, const void* kv, const int32_t* indices, void* 
     p.chunk = static_cast<int>((topk + s - 1) / s);
     p.c = sm_scale * 1.4426950408889634f;
     p.kv_scale = kv_dtype == GLM53_KV_BF16 ? 1.0f : kv_scale;
-    p.timeout_ns = g_timeout_ns;
+    p.timeout_ns = g_timeout_ns.load();
     cudaError_t e;
     if (H <= 16)
       e = fp8 ? launch_fwd<16, true>(p, s, st) : launch_fwd<16, false>(p, s, st);
@@ -1470,6 +1537,11 @@ extern "C" int glm53_sparse_mla_fwd_noalloc(const void* q, const void* kv, const
                         stream);
 }
 
+extern "C" int glm53_sparse_mla_set_wait_timeout_ns(uint64_t ns) {
+  g_timeout_ns.store(ns > 0 ? static_cast<unsigned long long>(ns) : default_timeout_ns());
+  return GLM53_OK;
+}
+
 extern "C" int glm53_sparse_mla_device_status(uint32_t* status, int clear) {
   unsigned int v = 0;
   if (cudaMemcpyFromSymbol(&v, g_device_status, sizeof(v)) != cudaSuccess) return GLM53_ERR_CUDA;
@@ -1483,16 +1555,18 @@ extern "C" int glm53_sparse_mla_device_status(uint32_t* status, int clear) {
 }
 
 extern "C" int glm53_gather_roof(const void* kv, const int32_t* indices, int64_t T, int64_t topk,
-                                 int64_t kv_rows, void* sink, void* stream) {
-  if (T < 0 || topk < 0 || kv_rows < 0) return GLM53_ERR_RANK;
+                                 int64_t kv_rows, int ctas, uint32_t* sink, void* stream) {
+  if (T < 0 || topk < 0 || kv_rows < 0 || ctas < 0) return GLM53_ERR_RANK;
   if (T == 0 || topk == 0) return GLM53_OK;
   if (kv == nullptr || indices == nullptr || !aligned16(kv)) return GLM53_ERR_ALIGN;
   const int rc = prepare_current_device(nullptr);
   if (rc != GLM53_OK) return rc;
-  gather_roof_kernel<<<static_cast<unsigned>(T), 256, 2 * kStageBytes + 1024,
+  const long long total = T * topk;
+  const long long grid = ctas == 0 ? T : std::min<long long>(ctas, total);
+  const long long per_cta = (total + grid - 1) / grid;
+  gather_roof_kernel<<<static_cast<unsigned>(grid), kRoofThreads, kRoofStages * kStageBytes + 1024,
                        static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint8_t*>(kv), indices, static_cast<int>(topk), kv_rows,
-      static_cast<uint32_t*>(sink));
+      static_cast<const uint8_t*>(kv), indices, total, per_cta, kv_rows, sink);
   return cudaGetLastError() == cudaSuccess ? GLM53_OK : GLM53_ERR_CUDA;
 }
 
