@@ -86,20 +86,37 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
                : "memory");
 }
 
+// As mbar_try_wait, with the suspension of the waiting thread capped at
+// `hint_ns` nanoseconds (PTX suspendTimeHint) instead of the hardware's own
+// limit, so a caller regains control at least that often.
+__device__ __forceinline__ bool mbar_try_wait_for(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for the phase with the given parity to complete, but never forever:
 // after `timeout_ns` of wall time (or as soon as another role of the CTA has
 // raised `abort_flag`) give up, raise the flag and return false. Callers then
 // skip the rest of their work but still take every CTA / cluster barrier, so a
-// pipeline bug turns into an error status instead of a hung GPU.
+// pipeline bug turns into an error status instead of a hung GPU. Each try
+// suspends the thread for at most min(timeout_ns, 20 us), so the limit and
+// the abort flag are checked at least that often, whatever the hardware's own
+// suspension limit is.
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
                                                   volatile int* abort_flag,
                                                   uint64_t timeout_ns) {
-  if (mbar_try_wait(bar, parity)) return true;
+  const uint32_t hint = timeout_ns < 20000u ? static_cast<uint32_t>(timeout_ns) : 20000u;
+  if (mbar_try_wait_for(bar, parity, hint)) return true;
   const uint64_t t0 = global_timer_ns();
   while (true) {
-#pragma unroll 1
-    for (int i = 0; i < 32; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_for(bar, parity, hint)) return true;
     if (*abort_flag) return false;
     if (global_timer_ns() - t0 > timeout_ns) {
       *abort_flag = 1;
