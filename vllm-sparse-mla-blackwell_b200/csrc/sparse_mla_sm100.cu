@@ -6,8 +6,10 @@
 // Work decomposition
 //   grid.x = T * splits. The `splits` CTAs of one token form a thread-block
 //   cluster and each takes a contiguous chunk of the token's index list; their
-//   partial results are merged through distributed shared memory at the end,
-//   so no global scratch and no second launch are needed.
+//   partial results are merged at the end of the same launch, either through a
+//   global workspace that stays in L2 (glm53_sparse_mla_fwd_ws, the torch op,
+//   the no-allocation entry point) or through distributed shared memory
+//   (glm53_sparse_mla_fwd, no global scratch).
 //
 // Per CTA (384 threads, one CTA per SM, ~222 KB shared memory)
 //   warps 0-3   softmax, GEMM2 issue, epilogue (warp w owns TMEM lanes 32w..)
@@ -31,8 +33,8 @@
 //          N=NH (heads), K=64; A=KV read MN-major from the same smem tile,
 //          B=P K-major; O^T accumulates in TMEM across all tiles. The four
 //          d-chunks are issued interleaved so consecutive UMMAs are independent.
-// UMMAs are issued in short straight-line bursts by five threads: warp 7
-// issues GEMM1(t) as soon as tile t's rows have landed; once P(t) is written,
+// UMMAs are issued in short straight-line bursts by five threads: lane 0 of
+// warp 11 issues GEMM1(t) as soon as tile t's rows have landed; once P(t) is written,
 // each softmax warp issues the 4 K-steps of one d-chunk of GEMM2(t). The
 // tensor pipe interleaves the streams, so the GEMM2 that frees a stage never
 // waits for a whole GEMM1 burst.
@@ -53,11 +55,13 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_fp8.h>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
 #include <atomic>
 #include <cmath>
+#include <cstring>
 #include <cstdint>
 #include <cstdlib>
 #include <mutex>
@@ -119,7 +123,7 @@ enum : int {
   kBarSEmpty = 8,    // [2] softmax -> GEMM1 issuer: S buffer read
   kBarODone = 10,    // GEMM2 (4 commits) -> softmax: a GEMM2 finished
   kBarDrain = 11,    // GEMM1 issuer's UMMAs all retired
-  kBarQFull = 12,    // all threads (cp.async) -> GEMM1 issuer: Q landed
+  kBarQFull = 12,    // Q landed (bf16: TMA transaction count; fp8: all threads) -> GEMM1 issuer
   kBarKvFirst = 13,  // [2] all threads -> GEMM1 issuer: tile 0 / 1 loaded
   kBarG2Drain = 15,  // [4] GEMM2 issuer of softmax warp w: its UMMAs all retired
   kNumBars = 19
@@ -208,7 +212,8 @@ __device__ __forceinline__ void store_pairs_n(__nv_bfloat16* o_tok, int H, int d
 }
 
 template <int NH, bool kFp8>
-__global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __grid_constant__ Params p) {
+__global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __grid_constant__ Params p,
+                                                                 const __grid_constant__ CUtensorMap q_map) {
   static_assert(NH == 16 || NH == 32 || NH == 64, "padded head count");
   using L = Lay<NH>;
   constexpr int kStages = L::kStages;
@@ -251,7 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
     }
     mbar_init(bar(kBarODone), 4);
     mbar_init(bar(kBarDrain), 1);
-    mbar_init(bar(kBarQFull), kThreads);
+    mbar_init(bar(kBarQFull), kFp8 ? kThreads : 1);
     mbar_init(bar(kBarKvFirst), kThreads);
     mbar_init(bar(kBarKvFirst + 1), kThreads);
     for (int w = 0; w < 4; ++w) mbar_init(bar(kBarG2Drain + w), 1);
@@ -266,6 +271,20 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
   // With programmatic dependent launch the set-up above overlaps the previous
   // grid's tail; nothing global is read or written before this point.
   griddep_wait();
+  // bf16: Q by TMA, 8 boxes of kQRows x 64 elements (128-byte swizzle, the
+  // operand layout), rows past H zero-filled by the tensor map's bounds
+  if constexpr (!kFp8) {
+    if (tid == 0) {
+      mbar_arrive_expect_tx(bar(kBarQFull), 8u * kQRows * 128u);
+#pragma unroll
+      for (int cb = 0; cb < 8; ++cb)
+        asm volatile(
+            "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+            "[%0], [%1, {%2, %3, %4}], [%5];" ::"r"(sb + kSmQ + cb * kQBlock),
+            "l"(reinterpret_cast<uint64_t>(&q_map)), "r"(cb * 64), "r"(0), "r"(token), "r"(bar(kBarQFull))
+            : "memory");
+    }
+  }
 
   // Index compaction, pass 1: warps 0-7 each take a contiguous sub-range of
   // this CTA's chunk, keep it in registers and count the valid entries.
@@ -304,13 +323,12 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
     if (lane == 0) misc[kMiscWarpCount + warp] = static_cast<uint32_t>(cnt);
     if (bad) atomicOr(&g_device_status, static_cast<unsigned>(GLM53_DEV_BAD_INDEX));
   }
-  // Q (the kQRows stored rows of the M=64 operand; rows >= H are zero), issued after
-  // the index loads so those are not queued behind it; its arrival is tracked
-  // by its own barrier so the KV gather never waits on it.
-  // bf16 KV: Q by cp.async as it is. fp8 KV (f16 datapath): Q through
-  // registers, converted to f16 with one power-of-two scale s_q per token
-  // that puts max |q * s_q| in [2^13, 2^14): exact for every bf16 value in
-  // range, never overflowing; 1 / s_q is folded into the softmax scale.
+  // fp8 KV (f16 datapath): Q (the kQRows stored rows of the M=64 operand; rows
+  // >= H are zero) through registers, converted to f16 with one power-of-two
+  // scale s_q per token that puts max |q * s_q| in [2^13, 2^14): exact for
+  // every bf16 value in range, never overflowing; 1 / s_q is folded into the
+  // softmax scale. Issued after the index loads so those are not queued
+  // behind it.
   constexpr int kQPer = (kQRows * 64 + kThreads - 1) / kThreads;
   uint4 qv[kFp8 ? kQPer : 1];
   float s_q = 1.f;
@@ -332,14 +350,6 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
 #pragma unroll
     for (int k = 16; k >= 1; k >>= 1) qmax = fmaxf(qmax, __shfl_xor_sync(0xFFFFFFFFu, qmax, k));
     if (lane == 0) alpha_sm[warp] = qmax;   // alpha_sm is free until the softmax
-  } else {
-    const __nv_bfloat16* qtok = p.q + static_cast<size_t>(token) * p.H * kDim;
-    for (int u = tid; u < kQRows * 64; u += kThreads) {
-      const int h = u >> 6, c = u & 63;
-      const bool ok = h < p.H;
-      cp_async_16(sb + kSmQ + swz<kQBlock>(h, c), qtok + (ok ? h : 0) * kDim + c * 8, ok ? 16u : 0u);
-    }
-    cp_async_mbar_arrive_noinc(bar(kBarQFull));
   }
   __syncthreads();
   if constexpr (kFp8) {
@@ -1206,8 +1216,49 @@ unsigned long long default_timeout_ns() {
 }
 int g_env_splits = -1;   // GLM53_SPLITS: forced split count for splits == 0 (-1: unread)
 
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// The driver's tensor-map encoder, fetched once through the runtime (the
+// library links only the CUDA runtime).
+EncodeTiledFn q_encoder() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// Tensor map of q [T, H, 512] bf16 viewed as the 3-D tensor {512, H, T}, boxes
+// of {64 elements, rows heads, 1 token} with the 128-byte swizzle: one box is
+// one 64-element column block of GEMM1's A operand. Heads past H read as zero
+// (the box leaves the tensor), which pads Q to the kernel's head count.
+bool make_q_map(CUtensorMap* map, const void* q, int64_t T, int64_t H, int rows) {
+  EncodeTiledFn enc = q_encoder();
+  if (enc == nullptr) return false;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kDim), static_cast<cuuint64_t>(H),
+                              static_cast<cuuint64_t>(T)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(kDim * 2), static_cast<cuuint64_t>(H * kDim * 2)};
+  const cuuint32_t box[3] = {64u, static_cast<cuuint32_t>(rows), 1u};
+  const cuuint32_t elem[3] = {1u, 1u, 1u};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(q), dims, strides, box, elem,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int NH, bool FP8>
 cudaError_t launch_fwd(const Params& p, int splits, cudaStream_t stream) {
+  CUtensorMap q_map;
+  std::memset(&q_map, 0, sizeof(q_map));
+  if (!FP8 && !make_q_map(&q_map, p.q, p.T, p.H, static_cast<int>(Lay<NH>::kQRows)))
+    return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(p.T) * static_cast<unsigned>(splits), 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
@@ -1222,7 +1273,7 @@ cudaError_t launch_fwd(const Params& p, int splits, cudaStream_t stream) {
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = splits > 1 ? 2 : 1;
-  return cudaLaunchKernelEx(&cfg, sparse_mla_fwd_kernel<NH, FP8>, p);
+  return cudaLaunchKernelEx(&cfg, sparse_mla_fwd_kernel<NH, FP8>, p, q_map);
 }
 
 template <int NH, bool FP8>
