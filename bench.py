@@ -103,6 +103,9 @@ def parse_args():
     ap.add_argument("--no-clocks", action="store_true")
     ap.add_argument("--no-spread", action="store_true", help="skip the median / p10 / p90 replays")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the extra keys of the default line (the other configs, the "
+                         "reference's GPU kernel, the W_UV projection)")
     return ap.parse_args()
 
 
@@ -360,6 +363,90 @@ def gather_roof_ms(G, sets, stream, n_steps: int):
     return graph_ms(step, n_steps, stream)
 
 
+def extra_configs(args, G, W, device, stream, hbm_peak: float) -> dict:
+    """The other benchmark configurations, timed the same way as the headline
+    (a CUDA graph of back-to-back launches over rotating input sets, CUDA
+    events): C3 mixed prefill + decode, C4 fp8 decode, C5 MTP with bf16 and
+    fp8 KV. Each reports ms per step, query-tokens/s and the fraction of the
+    HBM roofline (algorithmic bytes / time / measured copy bandwidth)."""
+    out = {}
+    for key, mk, n_sets, steps in (
+            ("c3", lambda s: W.config_c3(device=device, seed=s), 2, 6),
+            ("c4_fp8", lambda s: W.config_c4(device=device, seed=s), 8, 50),
+            ("c5_bf16", lambda s: W.config_c5(device=device, seed=s, heads=64), 2, 10),
+            ("c5_fp8", lambda s: W.config_c5(device=device, seed=s, heads=64, kv_dtype="fp8"), 2, 10)):
+        sets = [mk(200 + s) for s in range(n_sets)]
+        outs = [torch.empty_like(w.q) for w in sets]
+
+        def step(k):
+            w = sets[k % n_sets]
+            torch.ops.glm53_sparse_mla.sparse_fwd(w.q, w.kv, w.indices, w.sm_scale, w.kv_scale,
+                                                  outs[k % n_sets])
+        ms = graph_ms(step, steps, stream)
+        w = sets[0]
+        ab = w.algorithmic_bytes()
+        out[key] = {"ms_per_step": round(ms, 5), "value": round(w.T / (ms / 1e3), 1),
+                    "unit": UNIT, "tokens": w.T, "heads": w.H,
+                    "kv_dtype": "fp8_e4m3" if w.kv.dtype == torch.float8_e4m3fn else "bf16",
+                    "frac": round(ab / (ms / 1e3) / 1e9 / hbm_peak, 4),
+                    "algorithmic_bytes_per_launch": ab, "sets": n_sets}
+        del sets, outs
+        torch.cuda.empty_cache()
+    return out
+
+
+def reference_gpu_leg(timeout_s: float = 240.0):
+    """Comparator: the reference's own kernel (csrc/sparse_mla.cu, built for
+    sm_100a into oracle/_ref/ by oracle/build_ref.py) timed on the same
+    workloads in a separate process (it registers the same op namespace). A
+    baseline, never this repository's number; None when it was not built."""
+    so = os.path.join(REPO, "oracle", "_ref", "ref_sparse_mla_sm100.so")
+    if not os.path.exists(so):
+        return {"unavailable": "oracle/_ref not built"}
+    cmd = [sys.executable, os.path.join(REPO, "oracle", "ref_gpu_bench.py"),
+           "--workload", "c2,c4,c5,c5f,c3", "--steps", "50", "--warmup", "3"]
+    try:
+        res = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout_s, cwd=REPO)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": f"did not finish in {timeout_s:.0f} s"}
+    out = {}
+    for ln in res.stdout.splitlines():
+        try:
+            d = json.loads(ln)
+        except ValueError:
+            continue
+        if "workload" in d:
+            out[d["workload"]] = {"ms_per_step": d["ms_per_step"], "value": d["value"],
+                                  "launches_per_step": d["launches_per_step"]}
+    if not out:
+        return {"unavailable": (res.stderr or res.stdout)[-300:]}
+    out["kernel"] = "reference csrc/sparse_mla.cu (mma.sync), sm_100a build, 32 heads per launch"
+    return out
+
+
+def w_uv_leg(stream, device, attention_ms: dict) -> dict:
+    """The W_UV up-projection vLLM runs after this op (MLAAttention._v_up_proj:
+    out [T, H, 512] -> transpose -> batched GEMM with W_UV [H, 512, 128] ->
+    [T, H * 128]), timed at the C2 and C5 shapes next to the attention, with
+    random weights: the measured size of the work a fused epilogue would take
+    over."""
+    res = {}
+    for key, T in (("c2", 32), ("c5", 512)):
+        H = 64
+        x = torch.randn(T, H, 512, device=device).to(torch.bfloat16)
+        wuv = torch.randn(H, 512, 128, device=device).to(torch.bfloat16) * 0.05
+        y = torch.empty(T, H * 128, device=device, dtype=torch.bfloat16)
+
+        def step(k):
+            t = torch.bmm(x.transpose(0, 1), wuv)          # [H, T, 128]
+            y.view(T, H, 128).copy_(t.transpose(0, 1))
+        ms = graph_ms(step, 20, stream)
+        res[key] = {"w_uv_ms": round(ms, 5), "attention_ms": attention_ms.get(key),
+                    "w_uv_share": (round(ms / attention_ms[key], 4) if attention_ms.get(key) else None),
+                    "weights_bytes": H * 512 * 128 * 2}
+    return res
+
+
 def set_splits(n: int):
     if n:
         os.environ["GLM53_SPLITS"] = str(n)
@@ -502,6 +589,16 @@ def run_ours(args, dist: Dist):
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(w0, args.cpu_seconds)
 
+    # extra keys, after every timed loop of the contract: the other configs,
+    # the W_UV projection vLLM runs next, the reference's own GPU kernel
+    extras = {}
+    if not args.no_extras and dist.world == 1 and args.workload == "c2" and not args.heads:
+        extras["configs"] = extra_configs(args, G, W, device, stream, hbm_peak)
+        extras["w_uv"] = w_uv_leg(stream, device, {
+            "c2": ms_local / args.steps,
+            "c5": extras["configs"]["c5_bf16"]["ms_per_step"]})
+        extras["reference_gpu"] = reference_gpu_leg()
+
     if dist.rank == 0:
         cfg = attention_config(args, w0, heads_total, dist.world)
         line = {"metric": METRIC if args.workload == "c2" else f"sparse-MLA {UNIT} ({args.workload})",
@@ -513,6 +610,7 @@ def run_ours(args, dist: Dist):
                 "config": cfg, "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
                 "gpu_launches": args.steps + (args.steps if e2e else 0),
                 "clocks": clk.summary(), "spread": spread}
+        line.update(extras)
         print(json.dumps(line), flush=True)
     dist.close()
 

@@ -9,6 +9,7 @@ supports 8, 16 or 32 heads per launch (csrc/sparse_mla.cu:488-496), so a
 reference would serve 64 heads on one GPU (two ranks' worth of work).
 
     python oracle/ref_gpu_bench.py --workload c2 --steps 200 --warmup 10
+    python oracle/ref_gpu_bench.py --workload c2,c4,c5,c5f,c3
 """
 
 from __future__ import annotations
@@ -25,7 +26,9 @@ sys.path.insert(0, os.path.join(REPO, "vllm-sparse-mla-blackwell_b200"))
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5"], default="c2")
+    ap.add_argument("--workload", default="c2",
+                    help="c2, c3, c4, c5 or c5f (C5 with fp8 KV); a comma-separated list runs "
+                         "each in turn and prints one JSON line per workload")
     ap.add_argument("--heads", type=int, default=0)
     ap.add_argument("--kv", choices=["bf16", "fp8"], default="bf16")
     ap.add_argument("--steps", type=int, default=200)
@@ -49,11 +52,20 @@ def main():
     spec.loader.exec_module(W)
 
     dev = torch.device("cuda", 0)
+    for wl in args.workload.split(","):
+        run_one(args, W, torch, dev, wl)
+
+
+def run_one(args, W, torch, dev, wl):
+    kv = "fp8" if wl == "c5f" else args.kv
     mk = {"c2": lambda s: W.config_c2(device=dev, seed=s),
           "c3": lambda s: W.config_c3(device=dev, seed=s),
           "c4": lambda s: W.config_c4(device=dev, seed=s),
-          "c5": lambda s: W.config_c5(device=dev, seed=s, kv_dtype=args.kv)}[args.workload]
-    sets = [mk(100 + s) for s in range(args.sets)]
+          "c5": lambda s: W.config_c5(device=dev, seed=s, kv_dtype=kv),
+          "c5f": lambda s: W.config_c5(device=dev, seed=s, kv_dtype="fp8")}[wl]
+    n_sets = args.sets if wl in ("c2", "c4") else min(args.sets, 2)
+    steps = args.steps if wl in ("c2", "c4") else max(2, args.steps // 10)
+    sets = [mk(100 + s) for s in range(n_sets)]
     if args.heads:
         for w in sets:
             w.q = w.q[:, :args.heads].contiguous()
@@ -76,7 +88,7 @@ def main():
     torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g, stream=stream):
-        for k in range(args.steps):
+        for k in range(steps):
             step(k)
     g.replay()
     torch.cuda.synchronize()
@@ -86,14 +98,16 @@ def main():
         g.replay()
         e1.record(stream)
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / args.steps
+    ms = e0.elapsed_time(e1) / steps
     w = sets[0]
     print(json.dumps({"impl": "reference-gpu (csrc/sparse_mla.cu built for sm_100a)",
-                      "workload": args.workload, "heads": H, "launches_per_step": len(parts),
+                      "workload": wl, "heads": H, "launches_per_step": len(parts),
                       "tokens": w.T, "ms_per_step": round(ms, 5),
                       "value": round(w.T / (ms / 1e3), 1), "unit": "query-tokens/s",
                       "gathered_GBps": round(w.n_valid() * 512 * w.kv.element_size() * len(parts)
-                                             / (ms / 1e3) / 1e9, 1)}))
+                                             / (ms / 1e3) / 1e9, 1)}), flush=True)
+    del g, sets, qs, outs
+    torch.cuda.empty_cache()
 
 
 if __name__ == "__main__":
