@@ -447,6 +447,76 @@ def w_uv_leg(stream, device, attention_ms: dict) -> dict:
     return res
 
 
+def eager_ms(step, n_steps: int, stream) -> float:
+    """Device ms per step of `step(k)` launched eagerly (3 warm-up steps, then
+    n_steps between CUDA events on `stream`)."""
+    with torch.cuda.stream(stream):
+        for k in range(3):
+            step(k)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        a.record(stream)
+        for k in range(n_steps):
+            step(k)
+        b.record(stream)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / n_steps
+
+
+def head_shard_leg(S, W, device, stream, dist, steps: int = 10) -> dict:
+    """The north star's head-sharding sweep, on the MTP shape (C5: 128
+    sequences x 4 tokens, top-k 2048, bf16 KV): rank r of N serves heads
+    [r * 64 / N, (r + 1) * 64 / N) of the same batch, index lists and pool
+    replicated (vLLM TP). Times, max over ranks, launched eagerly:
+      kernel_ms    the op alone (this rank's heads, local output)
+      nccl_ms      the op, then NCCL all_gather_into_tensor and the head
+                   reorder copy into [T, 64, 512]
+      fused_ms     the op writing its heads straight into every rank's
+                   [T, 64, 512] buffer (symmetric memory, plain peer stores),
+                   then a symmetric-memory barrier: no all-gather, no copy
+    value = tokens / fused_ms (strong scaling: the same 512 tokens for every
+    N). Every rank gathers the same KV bytes whatever its head count (one
+    latent head), so per-GPU time stays nearly flat as N grows."""
+    world, rank = dist.world, dist.rank
+    h0, h = S.head_range(rank, world, 64)
+    sets = [W.config_c5(device=device, seed=300 + s, heads=64) for s in range(2)]
+    qs = [w.q[:, h0:h0 + h].contiguous() for w in sets]
+    outs = [torch.empty_like(q) for q in qs]
+    op = torch.ops.glm53_sparse_mla.sparse_fwd
+
+    def kstep(k):
+        w = sets[k % 2]
+        op(qs[k % 2], w.kv, w.indices, w.sm_scale, w.kv_scale, outs[k % 2])
+
+    res = {"workload": "C5 MTP: 128 seqs x 4 tokens, topk 2048, ctx 32768, bf16 KV",
+           "tokens": sets[0].T, "heads_total": 64, "heads_per_gpu": h, "n_gpus": world,
+           "kv_bytes_per_gpu": sets[0].n_valid() * 1024}
+    res["kernel_ms"] = round(dist.max(eager_ms(kstep, steps, stream), device), 5)
+    if world == 1:
+        res["fused_ms"] = res["kernel_ms"]
+    else:
+        staging = torch.empty(world, sets[0].T, h, 512, dtype=torch.bfloat16, device=device)
+
+        def nstep(k):
+            kstep(k)
+            S.gather_heads(outs[k % 2], world, staging=staging)
+        res["nccl_ms"] = round(dist.max(eager_ms(nstep, steps, stream), device), 5)
+        gather = S.HeadShardGather(sets[0].T, 64, device=device)
+
+        def fstep(k):
+            w = sets[k % 2]
+            gather(qs[k % 2], w.kv, w.indices, w.sm_scale, w.kv_scale)
+        res["fused_ms"] = round(dist.max(eager_ms(fstep, steps, stream), device), 5)
+        dist.barrier()
+        del gather
+    res["value"] = round(sets[0].T / (res["fused_ms"] / 1e3), 1)
+    res["unit"] = UNIT
+    del sets, qs, outs
+    torch.cuda.empty_cache()
+    return res
+
+
 def set_splits(n: int):
     if n:
         os.environ["GLM53_SPLITS"] = str(n)
@@ -598,6 +668,8 @@ def run_ours(args, dist: Dist):
             "c2": ms_local / args.steps,
             "c5": extras["configs"]["c5_bf16"]["ms_per_step"]})
         extras["reference_gpu"] = reference_gpu_leg()
+    if not args.no_extras and args.workload == "c2" and not args.heads and args.shard == "tokens":
+        extras["head_shard"] = head_shard_leg(S, W, device, stream, dist)
 
     if dist.rank == 0:
         cfg = attention_config(args, w0, heads_total, dist.world)

@@ -115,6 +115,32 @@ int glm53_sparse_mla_fwd_ws(const void* q, const void* kv, const int32_t* indice
                             uint64_t workspace_bytes, void* stream);
 
 /*
+ * As glm53_sparse_mla_fwd_ws, for one rank of a head-sharded group (vLLM
+ * tensor parallelism: each rank serves H of heads_total heads of every
+ * token): the kernel writes its output directly into every rank's full
+ * output. outs is a HOST array of n_outs (1..8) device pointers, each to a
+ * bf16 [T, heads_total, 512] buffer (16-byte aligned) that this GPU can
+ * store to: its own, and the other ranks' buffers mapped into this process
+ * (CUDA IPC or symmetric memory, peer access over NVLink). This launch's H
+ * heads land at heads [head_offset, head_offset + H) of each buffer, with
+ * plain stores from the epilogue, so the output exchange overlaps the rest of
+ * the kernel and no all-gather or reorder copy follows. The caller
+ * synchronises the ranks after the launch (a barrier on the same stream)
+ * before reading the gathered buffers. Requires head_offset + H <=
+ * heads_total <= 512.
+ * Replaces the output all-gather a tensor-parallel caller would run after the
+ * reference op (csrc/sparse_mla.cu:455-505 serves one rank's heads and
+ * returns them in a [T, H, 512] tensor of its own).
+ */
+int glm53_sparse_mla_fwd_heads_gather(const void* q, const void* kv, const int32_t* indices,
+                                      void* const* outs, int n_outs, int64_t head_offset,
+                                      int64_t heads_total, float* lse, int64_t T, int64_t H,
+                                      int64_t head_dim, int64_t kv_rows, int64_t kv_width,
+                                      int64_t topk, int kv_dtype, float sm_scale, float kv_scale,
+                                      int splits, void* workspace, uint64_t workspace_bytes,
+                                      void* stream);
+
+/*
  * As glm53_sparse_mla_fwd_ws, with the index list in vLLM's request-local
  * form: topk_positions[t][k] (row stride positions_row_stride >= topk, only
  * the first topk columns read) is a token position within request

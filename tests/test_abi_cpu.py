@@ -167,3 +167,42 @@ def test_paged_entry_validates_before_cuda(lib):
     assert call(kv_rows=1 << 31) == E_RANK        # slots must fit int32
     assert call(T=0) == OK                        # nothing to do
     assert call() == E_ALIGN                      # null pointers, still no CUDA call
+
+
+GATHER_ARGS = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+               ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p] + [ctypes.c_int64] * 6 + [
+               ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_int, ctypes.c_void_p,
+               ctypes.c_uint64, ctypes.c_void_p]
+
+
+def test_heads_gather_entry_validates_before_cuda(lib):
+    """The fused head gather refuses a bad output set before any CUDA call
+    (fake, aligned, never dereferenced addresses stand in for device ones)."""
+    f = lib.glm53_sparse_mla_fwd_heads_gather
+    f.argtypes = GATHER_ARGS
+    f.restype = ctypes.c_int
+    fake = 0x10000
+
+    def call(n_outs=2, head_offset=0, heads_total=64, H=32, ptrs=(fake, fake + 4096)):
+        arr = (ctypes.c_void_p * 8)(*ptrs)
+        return f(fake, fake, fake, arr, n_outs, head_offset, heads_total, None, 4, H, 512, 4096,
+                 512, 64, 0, 0.1, 1.0, 0, None, 0, None)
+
+    assert call(n_outs=0) == 1                        # GLM53_ERR_RANK
+    assert call(n_outs=9) == 1
+    assert call(head_offset=40) == 1                  # 40 + 32 heads > 64
+    assert call(heads_total=16, H=32) == 1
+    assert call(ptrs=(fake, 0)) == 6                  # null output: GLM53_ERR_ALIGN
+    assert call(ptrs=(fake, fake + 8)) == 6           # misaligned output
+    assert call(H=12) == 3                            # heads per launch not served
+
+
+def test_fake_gather_heads_traces():
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    with FakeTensorMode():
+        q = torch.empty(4, 16, 512, dtype=torch.bfloat16, device="cuda")
+        kv = torch.empty(1024, 512, dtype=torch.bfloat16, device="cuda")
+        idx = torch.empty(4, 2048, dtype=torch.int32, device="cuda")
+        out = torch.empty(4, 64, 512, dtype=torch.bfloat16, device="cuda")
+        torch.ops.glm53_sparse_mla.sparse_fwd_gather_heads(q, kv, idx, 0.04, 1.0, [1024], 0, 16,
+                                                           out)

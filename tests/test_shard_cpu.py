@@ -80,3 +80,15 @@ def test_ranges():
     spans = [S.token_range(r, 3, 10) for r in range(3)]
     assert spans == [(0, 4), (4, 3), (7, 3)]
     assert S.token_range(3, 4, 2) == (2, 0)
+
+
+def test_peer_pointer_order():
+    assert S.peer_pointer_order([4096, 8192], 1) == [4096, 8192]
+    with pytest.raises(ValueError):
+        S.peer_pointer_order([], 0)
+    with pytest.raises(ValueError):
+        S.peer_pointer_order([16] * 9, 0)
+    with pytest.raises(ValueError):
+        S.peer_pointer_order([4096, 8192], 2)
+    with pytest.raises(ValueError):
+        S.peer_pointer_order([4096, 8200], 0)          # not 16-byte aligned

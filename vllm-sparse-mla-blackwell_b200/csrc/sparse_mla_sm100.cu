@@ -82,6 +82,7 @@ constexpr int kProducerWarp0 = 4;   // warps 4-10 gather
 constexpr int kProducerWarps = 7;
 constexpr int kProducerThreads = 32 * kProducerWarps;
 constexpr int kMmaWarp = 11;
+constexpr int kMaxOutputs = 8;      // ranks of a head-sharded group written by one launch
 constexpr int kTmemCols = 512;
 constexpr uint32_t kTmemS = 256;    // S double buffer at columns 256 and 320
 constexpr float kRescaleThreshold = 8.0f;   // log2 units: rescale when max grows > 256x
@@ -151,7 +152,14 @@ struct Params {
   long long idx_stride;
   long long bt_stride;
   int max_blocks, block_size, block_stride;
-  __nv_bfloat16* out;       // [T, H, 512]
+  // Outputs: n_out buffers (1 for the plain forward; one per rank of a
+  // head-sharded group, possibly on other GPUs, for the fused head gather).
+  // Output i of token t, head h (h < H), element d is
+  // outs[i][t * out_tok_stride + h * 512 + d]; the head offset of this rank's
+  // shard is folded into the base pointers.
+  __nv_bfloat16* outs[kMaxOutputs];
+  int n_out;
+  long long out_tok_stride;
   float* lse;               // [T, H] or nullptr
   float* ws;                // split-merge workspace (see the merge), or nullptr
   long long kv_rows;
@@ -195,10 +203,25 @@ __device__ __forceinline__ uint4 dequant8(const uint2 w) {
                     e4m3x2_to_f16x2(w.y & 0xFFFFu), e4m3x2_to_f16x2(w.y >> 16));
 }
 
+// Write one bf16x2 (elements d_even, d_even + 1 of head hw of token `token`)
+// to every output buffer: plain stores, to peer GPUs' memory for the outputs
+// of a head-sharded group.
+__device__ __forceinline__ void store_out_pair(const Params& p, int token, int hw, int d_even,
+                                               uint32_t pair) {
+  const size_t off = static_cast<size_t>(token) * p.out_tok_stride + static_cast<size_t>(hw) * kDim + d_even;
+  if (p.n_out == 1) {
+    *reinterpret_cast<uint32_t*>(p.outs[0] + off) = pair;
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < kMaxOutputs; ++i)   // constant indices: read straight from the parameters
+    if (i < p.n_out) *reinterpret_cast<uint32_t*>(p.outs[i] + off) = pair;
+}
+
 // bf16 store of out[h0 + j][d] for j < N: neighbouring lanes (d, d ^ 1) swap
 // one value per head pair so each lane writes a bf16x2 of two adjacent d.
 template <int N>
-__device__ __forceinline__ void store_pairs_n(__nv_bfloat16* o_tok, int H, int d, int h0,
+__device__ __forceinline__ void store_pairs_n(const Params& p, int token, int d, int h0,
                                               const float (&o)[N]) {
   const bool odd = threadIdx.x & 1;
   const int d_even = d & ~1;
@@ -207,7 +230,7 @@ __device__ __forceinline__ void store_pairs_n(__nv_bfloat16* o_tok, int H, int d
     const float recv = __shfl_xor_sync(0xFFFFFFFFu, odd ? o[j] : o[j + 1], 1);
     const int hw = h0 + (odd ? j + 1 : j);
     const uint32_t pair = odd ? pack_bf16x2(recv, o[j + 1]) : pack_bf16x2(o[j], recv);
-    if (hw < H) *reinterpret_cast<uint32_t*>(o_tok + static_cast<size_t>(hw) * kDim + d_even) = pair;
+    if (hw < p.H) store_out_pair(p, token, hw, d_even, pair);
   }
 }
 
@@ -729,7 +752,6 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
   // may start launching (its CTAs wait in griddep_wait for this one to end).
   griddep_launch_dependents();
   const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
-  __nv_bfloat16* const o_tok = p.out + static_cast<size_t>(token) * p.H * kDim;
   const bool odd = lane & 1;
 
   // O^T[d][0..NH) of TMEM lane d of chunk m (all loads issued, one wait)
@@ -757,8 +779,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
       const float recv = __shfl_xor_sync(0xFFFFFFFFu, odd ? o[j] : o[j + 1], 1);
       const int hw = odd ? j + 1 : j;
       const uint32_t pair = odd ? pack_bf16x2(recv, o[j + 1]) : pack_bf16x2(o[j], recv);
-      if (hw < p.H)
-        *reinterpret_cast<uint32_t*>(o_tok + static_cast<size_t>(hw) * kDim + d_even) = pair;
+      if (hw < p.H) store_out_pair(p, token, hw, d_even, pair);
     }
   };
 
@@ -889,7 +910,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
           }
 #pragma unroll
           for (int j = 0; j < 16; ++j) o[j] *= scal[8 * NH + hb + j];
-          store_pairs_n<16>(o_tok, p.H, d, hb, o);
+          store_pairs_n<16>(p, token, d, hb, o);
         }
       }
     }
@@ -1041,7 +1062,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
           }
 #pragma unroll
           for (int j = 0; j < 16; ++j) o[j] *= scal[4 * NH + hb + j];
-          store_pairs_n<16>(o_tok, p.H, d, hb, o);
+          store_pairs_n<16>(p, token, d, hb, o);
         }
       }
       tc_fence_before();
@@ -1107,9 +1128,12 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
         acc[0] += x[r].x; acc[1] += x[r].y; acc[2] += x[r].z; acc[3] += x[r].w;
         acc[4] += y[r].x; acc[5] += y[r].y; acc[6] += y[r].z; acc[7] += y[r].w;
       }
-      stg_v4(o_tok + static_cast<size_t>(hh) * kDim + d,
-             make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
-                        pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7])));
+      const uint4 v = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
+                                 pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
+      const size_t o_off = static_cast<size_t>(token) * p.out_tok_stride + static_cast<size_t>(hh) * kDim + d;
+#pragma unroll
+      for (int i = 0; i < kMaxOutputs; ++i)
+        if (i < p.n_out) stg_v4(p.outs[i] + o_off, v);
     }
     cluster_sync_all();   // (C) no CTA leaves while a peer still reads its smem
   }
@@ -1403,15 +1427,23 @@ struct Paged {
   int64_t idx_stride, bt_stride, max_blocks, block_size, block_stride;
 };
 
+// Output set of the fused head gather: n buffers [T, heads_total, 512], this
+// launch's H heads written at heads [head_offset, head_offset + H) of each.
+struct OutSet {
+  void* const* outs;
+  int n;
+  int64_t heads_total, head_offset;
+};
+
 // Shared body of the forward entry points. `ws == nullptr` selects the
 // distributed-shared-memory split merge; otherwise `ws` (at least
 // `ws_bytes`) is the global workspace of the L2 split merge. `pg` selects the
-// paged index form.
+// paged index form, `os` the outputs of a head-sharded group (else `out`).
 int launch_forward(const void* q, const void* kv, const int32_t* indices, void* out, float* lse,
                    int64_t T, int64_t H, int64_t head_dim, int64_t kv_rows, int64_t kv_width,
                    int64_t topk, int kv_dtype, float sm_scale, float kv_scale, int splits,
                    bool use_ws, void* ws, uint64_t ws_bytes, void* stream,
-                   const Paged* pg = nullptr) {
+                   const Paged* pg = nullptr, const OutSet* os = nullptr) {
   // A named host range for profilers and tracers (a no-op without one).
   struct NvtxRange {
     NvtxRange() { nvtxRangePushA("glm53_sparse_mla_fwd"); }
@@ -1426,6 +1458,14 @@ int launch_forward(const void* q, const void* kv, const int32_t* indices, void* 
       q == nullptr || kv == nullptr || indices == nullptr || out == nullptr)
     return GLM53_ERR_ALIGN;
   if (lse != nullptr && (reinterpret_cast<uintptr_t>(lse) & 3u) != 0) return GLM53_ERR_ALIGN;
+  void* const single[1] = {out};
+  const OutSet one{single, 1, H, 0};
+  if (os == nullptr) os = &one;
+  if (os->n < 1 || os->n > kMaxOutputs || os->outs == nullptr || os->head_offset < 0 ||
+      os->head_offset + H > os->heads_total || os->heads_total > 64 * kMaxOutputs)
+    return GLM53_ERR_RANK;
+  for (int i = 0; i < os->n; ++i)
+    if (os->outs[i] == nullptr || !aligned16(os->outs[i])) return GLM53_ERR_ALIGN;
   int dev = 0;
   rc = prepare_current_device(&dev);
   if (rc != GLM53_OK) return rc;
@@ -1456,7 +1496,12 @@ int launch_forward(const void* q, const void* kv, const int32_t* indices, void* 
     p.max_blocks = pg != nullptr ? static_cast<int>(pg->max_blocks) : 0;
     p.block_size = pg != nullptr ? static_cast<int>(pg->block_size) : 1;
     p.block_stride = pg != nullptr ? static_cast<int>(pg->block_stride) : 1;
-    p.out = static_cast<__nv_bfloat16*>(out) + t0 * q_tok;
+    for (int i = 0; i < kMaxOutputs; ++i)
+      p.outs[i] = i < os->n ? static_cast<__nv_bfloat16*>(os->outs[i]) +
+                                  (t0 * os->heads_total + os->head_offset) * kDim
+                            : nullptr;
+    p.n_out = os->n;
+    p.out_tok_stride = os->heads_total * kDim;
     p.lse = lse != nullptr ? lse + t0 * H : nullptr;
     p.ws = (use_ws && s > 1) ? ws_next : nullptr;
     if (p.ws != nullptr) ws_next += workspace_floats(n, H, s);
@@ -1540,6 +1585,18 @@ extern "C" int glm53_sparse_mla_fwd_ws(const void* q, const void* kv, const int3
   return launch_forward(q, kv, indices, out, lse, T, H, head_dim, kv_rows, kv_width, topk,
                         kv_dtype, sm_scale, kv_scale, splits, true, workspace, workspace_bytes,
                         stream);
+}
+
+extern "C" int glm53_sparse_mla_fwd_heads_gather(
+    const void* q, const void* kv, const int32_t* indices, void* const* outs, int n_outs,
+    int64_t head_offset, int64_t heads_total, float* lse, int64_t T, int64_t H, int64_t head_dim,
+    int64_t kv_rows, int64_t kv_width, int64_t topk, int kv_dtype, float sm_scale, float kv_scale,
+    int splits, void* workspace, uint64_t workspace_bytes, void* stream) {
+  if (outs == nullptr || n_outs < 1 || n_outs > kMaxOutputs) return GLM53_ERR_RANK;
+  const OutSet os{outs, n_outs, heads_total, head_offset};
+  return launch_forward(q, kv, indices, outs[0], lse, T, H, head_dim, kv_rows, kv_width, topk,
+                        kv_dtype, sm_scale, kv_scale, splits, true, workspace, workspace_bytes,
+                        stream, nullptr, &os);
 }
 
 // ---------------------------------------------------------------------------

@@ -160,6 +160,59 @@ void sparse_fwd_paged(torch::Tensor q, torch::Tensor kv, torch::Tensor topk_posi
   TORCH_CHECK(rc == GLM53_OK, "glm53_sparse_mla: ", glm53_sparse_mla_strerror(rc));
 }
 
+// One rank of a head-sharded group writing its heads straight into every
+// rank's full output. `out` is this rank's own [T, heads_total, 512] buffer
+// (its pointer must be the entry of out_ptrs at index `rank`); out_ptrs are
+// the device pointers of all ranks' buffers as this GPU addresses them
+// (symmetric memory). The caller synchronises the ranks afterwards.
+void sparse_fwd_gather_heads(torch::Tensor q, torch::Tensor kv, torch::Tensor indices,
+                             double sm_scale, double kv_scale, std::vector<int64_t> out_ptrs,
+                             int64_t rank, int64_t head_offset, torch::Tensor out) {
+  TORCH_CHECK(q.is_cuda() && kv.is_cuda() && indices.is_cuda() && out.is_cuda(),
+              "glm53_sparse_mla: q, kv, indices and out must be CUDA tensors");
+  TORCH_CHECK(q.dim() == 3 && kv.dim() == 2 && indices.dim() == 2 && out.dim() == 3,
+              "glm53_sparse_mla: expected q [T, H, 512], kv [R, 512], indices [T, topk], "
+              "out [T, heads_total, 512]");
+  TORCH_CHECK(q.scalar_type() == torch::kBFloat16 && indices.scalar_type() == torch::kInt,
+              "glm53_sparse_mla: q must be bfloat16 and indices int32");
+  TORCH_CHECK(q.is_contiguous() && kv.is_contiguous() && indices.is_contiguous() &&
+                  out.is_contiguous() && out.scalar_type() == torch::kBFloat16,
+              "glm53_sparse_mla: q, kv, indices and out must be contiguous, out bfloat16");
+  TORCH_CHECK(q.size(2) == kDim && kv.size(1) == kDim && out.size(2) == kDim,
+              "expected kv_lora_rank ", kDim, " with qk_rope_head_dim 0 (NoPE)");
+  const int64_t T = q.size(0), H = q.size(1), topk = indices.size(1);
+  TORCH_CHECK(indices.size(0) == T && out.size(0) == T, "glm53_sparse_mla: T rows everywhere");
+  TORCH_CHECK(!out_ptrs.empty() && out_ptrs.size() <= 8 && rank >= 0 &&
+                  rank < static_cast<int64_t>(out_ptrs.size()) &&
+                  out_ptrs[rank] == reinterpret_cast<int64_t>(out.data_ptr()),
+              "glm53_sparse_mla: out_ptrs must list 1 to 8 buffers, out at index rank");
+  TORCH_CHECK(head_offset >= 0 && head_offset + H <= out.size(1),
+              "glm53_sparse_mla: heads [head_offset, head_offset + H) must lie in out");
+  if (T == 0) return;
+  int kv_dtype = -1;
+  if (kv.scalar_type() == torch::kBFloat16) kv_dtype = GLM53_KV_BF16;
+  else if (kv.scalar_type() == torch::kFloat8_e4m3fn) kv_dtype = GLM53_KV_FP8_E4M3;
+  TORCH_CHECK(kv_dtype >= 0, "kv must be bfloat16 or float8_e4m3fn, got ", kv.scalar_type());
+  const c10::cuda::CUDAGuard guard(q.device());
+  cudaStream_t stream = c10::cuda::getCurrentCUDAStream(q.get_device()).stream();
+  uint64_t ws_bytes = 0;
+  int rc = glm53_sparse_mla_workspace_bytes(T, H, topk, /*splits=*/0, &ws_bytes);
+  TORCH_CHECK(rc == GLM53_OK, "glm53_sparse_mla: ", glm53_sparse_mla_strerror(rc));
+  torch::Tensor ws;
+  if (ws_bytes > 0)
+    ws = torch::empty({static_cast<int64_t>(ws_bytes)},
+                      torch::TensorOptions().dtype(torch::kUInt8).device(q.device()));
+  void* ptrs[8];
+  for (size_t i = 0; i < out_ptrs.size(); ++i) ptrs[i] = reinterpret_cast<void*>(out_ptrs[i]);
+  rc = glm53_sparse_mla_fwd_heads_gather(
+      q.data_ptr(), kv.data_ptr(), indices.data_ptr<int32_t>(), ptrs,
+      static_cast<int>(out_ptrs.size()), head_offset, out.size(1), nullptr, T, H, q.size(2),
+      kv.size(0), kv.size(1), topk, kv_dtype, static_cast<float>(sm_scale),
+      static_cast<float>(kv_scale), /*splits=*/0, ws_bytes > 0 ? ws.data_ptr() : nullptr, ws_bytes,
+      static_cast<void*>(stream));
+  TORCH_CHECK(rc == GLM53_OK, "glm53_sparse_mla: ", glm53_sparse_mla_strerror(rc));
+}
+
 // Latent KV-cache write with the schema and argument meaning of vLLM's
 // _C_cache_ops::concat_and_cache_mla (vllm 0.22.0 vllm/_custom_ops.py:2613-2623)
 // for this path's geometry: kv_lora_rank 512, pe_dim 0. The token count is
@@ -320,6 +373,7 @@ TORCH_LIBRARY(glm53_sparse_mla, m) {
   m.def("sparse_fwd(Tensor q, Tensor kv, Tensor indices, float sm_scale, float kv_scale, Tensor(a!) out) -> ()");
   m.def("sparse_fwd_lse(Tensor q, Tensor kv, Tensor indices, float sm_scale, float kv_scale, Tensor(a!) out, Tensor(b!) lse) -> ()");
   m.def("sparse_fwd_paged(Tensor q, Tensor kv, Tensor topk_positions, Tensor req_id_per_token, Tensor block_table, int block_size, int topk, float sm_scale, float kv_scale, Tensor(a!) out, Tensor(b!)? lse=None, int block_stride_rows=0) -> ()");
+  m.def("sparse_fwd_gather_heads(Tensor q, Tensor kv, Tensor indices, float sm_scale, float kv_scale, int[] out_ptrs, int rank, int head_offset, Tensor(a!) out) -> ()");
   m.def("concat_and_cache_mla(Tensor kv_c, Tensor k_pe, Tensor(a!) kv_cache, Tensor slot_mapping, str kv_cache_dtype, Tensor scale) -> ()");
   m.def("top_k_per_row_decode(Tensor logits, int next_n, Tensor seq_lens, Tensor(a!) raw_topk_indices, int num_rows, int stride0, int stride1, int topk_tokens) -> ()");
   m.def("top_k_per_row_prefill(Tensor logits, Tensor cu_seqlen_ks, Tensor cu_seqlen_ke, Tensor(a!) raw_topk_indices, int num_rows, int stride0, int stride1, int topk_tokens) -> ()");
@@ -330,6 +384,7 @@ TORCH_LIBRARY_IMPL(glm53_sparse_mla, CUDA, m) {
   m.impl("sparse_fwd", &sparse_fwd);
   m.impl("sparse_fwd_lse", &sparse_fwd_lse);
   m.impl("sparse_fwd_paged", &sparse_fwd_paged);
+  m.impl("sparse_fwd_gather_heads", &sparse_fwd_gather_heads);
   m.impl("concat_and_cache_mla", &concat_and_cache_mla);
   m.impl("top_k_per_row_decode", &top_k_per_row_decode);
   m.impl("top_k_per_row_prefill", &top_k_per_row_prefill);

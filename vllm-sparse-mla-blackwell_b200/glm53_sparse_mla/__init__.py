@@ -270,3 +270,11 @@ def _fp8_paged_mqa_logits_fake(q, kv_cache, weights, context_lens, block_tables,
                                clean_logits, logits):
     torch._check(q.dim() == 4 and logits.dim() == 2)
     return None
+
+
+@torch.library.register_fake("glm53_sparse_mla::sparse_fwd_gather_heads")
+def _sparse_fwd_gather_heads_fake(q, kv, indices, sm_scale, kv_scale, out_ptrs, rank, head_offset,
+                                  out):
+    torch._check(q.dim() == 3 and kv.dim() == 2 and indices.dim() == 2 and out.dim() == 3)
+    torch._check(out.shape[0] == q.shape[0] and out.shape[2] == q.shape[2])
+    return None

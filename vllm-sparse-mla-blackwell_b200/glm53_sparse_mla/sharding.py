@@ -8,21 +8,28 @@ Two ways to spread a batch over ``world`` ranks:
   list and the latent KV pool replicated (the pool is one shared latent head,
   as vLLM TP replicates the MLA cache). Heads are independent, so a shard's
   output is exactly the matching slice of the full result;
-  :func:`gather_heads` reassembles ``[T, H, 512]`` with one all-gather.
+  :func:`gather_heads` reassembles ``[T, H, 512]`` with one all-gather, and
+  :class:`HeadShardGather` does without it: the kernel stores each rank's
+  heads straight into every rank's full output (symmetric memory over
+  NVLink), so the exchange overlaps the attention itself.
 * **token sharding** (data-parallel attention): rank r serves a contiguous
   range of query tokens with all heads.
 
-The attention kernel never communicates; the only collective is the optional
-output all-gather (NCCL on GPUs, gloo in the CPU tests).
+Attention itself needs no collective; the only exchange is the optional
+output gather (NCCL all-gather, gloo in the CPU tests, or the fused peer
+stores of :class:`HeadShardGather`).
 """
 
 from __future__ import annotations
+
+import os
 
 import torch
 
 from . import SUPPORTED_HEADS_PER_RANK
 
-__all__ = ["head_range", "token_range", "shard_heads", "gather_heads"]
+__all__ = ["head_range", "token_range", "shard_heads", "gather_heads", "HeadShardGather",
+           "peer_pointer_order"]
 
 
 def head_range(rank: int, world: int, heads_total: int) -> tuple[int, int]:
@@ -69,3 +76,64 @@ def gather_heads(out_shard: torch.Tensor, world: int, group=None,
     else:
         torch.distributed.all_gather_into_tensor(staging, out_shard.contiguous(), group=group)
     return staging.permute(1, 0, 2, 3).reshape(T, world * h, d)
+
+
+def peer_pointer_order(buffer_ptrs, rank: int) -> list[int]:
+    """Output pointers for the fused gather, in rank order (rank i's buffer
+    at index i, this rank's own at index ``rank``): at most 8 ranks."""
+    ptrs = [int(x) for x in buffer_ptrs]
+    if not 1 <= len(ptrs) <= 8:
+        raise ValueError(f"the fused head gather spans 1 to 8 ranks, got {len(ptrs)}")
+    if not 0 <= rank < len(ptrs):
+        raise ValueError(f"rank {rank} outside {len(ptrs)} buffers")
+    if any(p == 0 or p % 16 for p in ptrs):
+        raise ValueError("every output buffer must be a non-null 16-byte aligned device pointer")
+    return ptrs
+
+
+class HeadShardGather:
+    """Head-sharded attention with the output gather fused into the kernel.
+
+    Every rank holds a ``[tokens, heads_total, 512]`` bf16 buffer in symmetric
+    memory (``torch.distributed._symmetric_memory``), mapped into every other
+    rank's address space. A call runs this rank's heads through
+    ``torch.ops.glm53_sparse_mla.sparse_fwd_gather_heads``: the epilogue of the
+    attention kernel stores each output element into all ranks' buffers at
+    this rank's head offset (plain peer stores over NVLink, no multicast), so
+    the exchange overlaps the kernel's remaining work and no all-gather or
+    reorder copy follows. A symmetric-memory barrier on the same stream then
+    orders every rank's stores before anyone reads; the call returns this
+    rank's gathered buffer. The buffer is reused by the next call.
+
+    Collective: every rank of ``group`` constructs it and calls it in the
+    same order.
+    """
+
+    def __init__(self, tokens: int, heads_total: int, group=None, device=None):
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self.group = group if group is not None else dist.group.WORLD
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        self.head_offset, self.heads = head_range(self.rank, self.world, heads_total)
+        self.tokens, self.heads_total = tokens, heads_total
+        device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        # plain peer stores are all the gather uses; keep the buffer off any
+        # NVLink multicast object
+        os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
+        self.buf = symm_mem.empty(tokens, heads_total, 512, dtype=torch.bfloat16, device=device)
+        self.handle = symm_mem.rendezvous(self.buf, self.group.group_name)
+        self.ptrs = peer_pointer_order(self.handle.buffer_ptrs, self.rank)
+
+    def __call__(self, q_shard: torch.Tensor, kv: torch.Tensor, indices: torch.Tensor,
+                 sm_scale: float, kv_scale: float = 1.0, barrier: bool = True) -> torch.Tensor:
+        if q_shard.shape[0] != self.tokens or q_shard.shape[1] != self.heads:
+            raise ValueError(f"q shard must be [{self.tokens}, {self.heads}, 512], got "
+                             f"{tuple(q_shard.shape)}")
+        torch.ops.glm53_sparse_mla.sparse_fwd_gather_heads(
+            q_shard, kv, indices, float(sm_scale), float(kv_scale), self.ptrs, self.rank,
+            self.head_offset, self.buf)
+        if barrier:
+            self.handle.barrier(channel=0, timeout_ms=10000)
+        return self.buf
