@@ -206,13 +206,17 @@ __device__ __forceinline__ uint4 dequant8(const uint2 w) {
 // Write one bf16x2 (elements d_even, d_even + 1 of head hw of token `token`)
 // to every output buffer: plain stores, to peer GPUs' memory for the outputs
 // of a head-sharded group.
-__device__ __forceinline__ void store_out_pair(const Params& p, int token, int hw, int d_even,
-                                               uint32_t pair) {
-  const size_t off = static_cast<size_t>(token) * p.out_tok_stride + static_cast<size_t>(hw) * kDim + d_even;
-  if (p.n_out == 1) {
-    *reinterpret_cast<uint32_t*>(p.outs[0] + off) = pair;
+// kMulti is a separate kernel instantiation, so the single-output kernel
+// carries none of the multi-output code.
+// o_tok is output 0's base for this token.
+template <bool kMulti>
+__device__ __forceinline__ void store_out_pair(const Params& p, __nv_bfloat16* o_tok, int token, int hw,
+                                               int d_even, uint32_t pair) {
+  if constexpr (!kMulti) {
+    *reinterpret_cast<uint32_t*>(o_tok + static_cast<size_t>(hw) * kDim + d_even) = pair;
     return;
   }
+  const size_t off = static_cast<size_t>(token) * p.out_tok_stride + static_cast<size_t>(hw) * kDim + d_even;
 #pragma unroll
   for (int i = 0; i < kMaxOutputs; ++i)   // constant indices: read straight from the parameters
     if (i < p.n_out) *reinterpret_cast<uint32_t*>(p.outs[i] + off) = pair;
@@ -220,8 +224,8 @@ __device__ __forceinline__ void store_out_pair(const Params& p, int token, int h
 
 // bf16 store of out[h0 + j][d] for j < N: neighbouring lanes (d, d ^ 1) swap
 // one value per head pair so each lane writes a bf16x2 of two adjacent d.
-template <int N>
-__device__ __forceinline__ void store_pairs_n(const Params& p, int token, int d, int h0,
+template <int N, bool kMulti>
+__device__ __forceinline__ void store_pairs_n(const Params& p, __nv_bfloat16* o_tok, int token, int d, int h0,
                                               const float (&o)[N]) {
   const bool odd = threadIdx.x & 1;
   const int d_even = d & ~1;
@@ -230,11 +234,11 @@ __device__ __forceinline__ void store_pairs_n(const Params& p, int token, int d,
     const float recv = __shfl_xor_sync(0xFFFFFFFFu, odd ? o[j] : o[j + 1], 1);
     const int hw = h0 + (odd ? j + 1 : j);
     const uint32_t pair = odd ? pack_bf16x2(recv, o[j + 1]) : pack_bf16x2(o[j], recv);
-    if (hw < p.H) store_out_pair(p, token, hw, d_even, pair);
+    if (hw < p.H) store_out_pair<kMulti>(p, o_tok, token, hw, d_even, pair);
   }
 }
 
-template <int NH, bool kFp8>
+template <int NH, bool kFp8, bool kMulti>
 __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __grid_constant__ Params p,
                                                                  const __grid_constant__ CUtensorMap q_map) {
   static_assert(NH == 16 || NH == 32 || NH == 64, "padded head count");
@@ -751,6 +755,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
   // Every CTA of this grid is resident by now, so the next grid in the stream
   // may start launching (its CTAs wait in griddep_wait for this one to end).
   griddep_launch_dependents();
+  __nv_bfloat16* const o_tok = p.outs[0] + static_cast<size_t>(token) * p.out_tok_stride;
   const uint32_t lane_base = static_cast<uint32_t>(32 * (warp & 3)) << 16;
   const bool odd = lane & 1;
 
@@ -779,7 +784,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
       const float recv = __shfl_xor_sync(0xFFFFFFFFu, odd ? o[j] : o[j + 1], 1);
       const int hw = odd ? j + 1 : j;
       const uint32_t pair = odd ? pack_bf16x2(recv, o[j + 1]) : pack_bf16x2(o[j], recv);
-      if (hw < p.H) store_out_pair(p, token, hw, d_even, pair);
+      if (hw < p.H) store_out_pair<kMulti>(p, o_tok, token, hw, d_even, pair);
     }
   };
 
@@ -910,7 +915,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
           }
 #pragma unroll
           for (int j = 0; j < 16; ++j) o[j] *= scal[8 * NH + hb + j];
-          store_pairs_n<16>(p, token, d, hb, o);
+          store_pairs_n<16, kMulti>(p, o_tok, token, d, hb, o);
         }
       }
     }
@@ -1062,7 +1067,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
           }
 #pragma unroll
           for (int j = 0; j < 16; ++j) o[j] *= scal[4 * NH + hb + j];
-          store_pairs_n<16>(p, token, d, hb, o);
+          store_pairs_n<16, kMulti>(p, o_tok, token, d, hb, o);
         }
       }
       tc_fence_before();
@@ -1130,10 +1135,14 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
       }
       const uint4 v = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
                                  pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
-      const size_t o_off = static_cast<size_t>(token) * p.out_tok_stride + static_cast<size_t>(hh) * kDim + d;
+      if constexpr (!kMulti) {
+        stg_v4(o_tok + static_cast<size_t>(hh) * kDim + d, v);
+      } else {
+        const size_t o_off = static_cast<size_t>(token) * p.out_tok_stride + static_cast<size_t>(hh) * kDim + d;
 #pragma unroll
-      for (int i = 0; i < kMaxOutputs; ++i)
-        if (i < p.n_out) stg_v4(p.outs[i] + o_off, v);
+        for (int i = 0; i < kMaxOutputs; ++i)
+          if (i < p.n_out) stg_v4(p.outs[i] + o_off, v);
+      }
     }
     cluster_sync_all();   // (C) no CTA leaves while a peer still reads its smem
   }
@@ -1277,7 +1286,7 @@ bool make_q_map(CUtensorMap* map, const void* q, int64_t T, int64_t H, int rows)
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int NH, bool FP8>
+template <int NH, bool FP8, bool MULTI>
 cudaError_t launch_fwd(const Params& p, int splits, cudaStream_t stream) {
   CUtensorMap q_map;
   std::memset(&q_map, 0, sizeof(q_map));
@@ -1297,12 +1306,12 @@ cudaError_t launch_fwd(const Params& p, int splits, cudaStream_t stream) {
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = splits > 1 ? 2 : 1;
-  return cudaLaunchKernelEx(&cfg, sparse_mla_fwd_kernel<NH, FP8>, p, q_map);
+  return cudaLaunchKernelEx(&cfg, sparse_mla_fwd_kernel<NH, FP8, MULTI>, p, q_map);
 }
 
-template <int NH, bool FP8>
+template <int NH, bool FP8, bool MULTI = false>
 cudaError_t set_smem_attr() {
-  return cudaFuncSetAttribute(sparse_mla_fwd_kernel<NH, FP8>,
+  return cudaFuncSetAttribute(sparse_mla_fwd_kernel<NH, FP8, MULTI>,
                               cudaFuncAttributeMaxDynamicSharedMemorySize,
                               static_cast<int>(Lay<NH>::kSmemBytes));
 }
@@ -1334,6 +1343,12 @@ int prepare_current_device(int* dev_out) {
   if (e == cudaSuccess) e = set_smem_attr<16, true>();
   if (e == cudaSuccess) e = set_smem_attr<32, true>();
   if (e == cudaSuccess) e = set_smem_attr<64, true>();
+  if (e == cudaSuccess) e = set_smem_attr<16, false, true>();
+  if (e == cudaSuccess) e = set_smem_attr<32, false, true>();
+  if (e == cudaSuccess) e = set_smem_attr<64, false, true>();
+  if (e == cudaSuccess) e = set_smem_attr<16, true, true>();
+  if (e == cudaSuccess) e = set_smem_attr<32, true, true>();
+  if (e == cudaSuccess) e = set_smem_attr<64, true, true>();
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(gather_roof_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kRoofStages * kStageBytes + 1024));
@@ -1477,6 +1492,7 @@ int launch_forward(const void* q, const void* kv, const int32_t* indices, void* 
 
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool fp8 = kv_dtype == GLM53_KV_FP8_E4M3;
+  const bool multi = os->n > 1;
   const size_t q_tok = static_cast<size_t>(H) * kDim;   // bf16 elements per token of q / out
   float* ws_next = use_ws ? static_cast<float*>(ws) : nullptr;
   for (int part = 0; part < 2; ++part) {
@@ -1516,11 +1532,14 @@ int launch_forward(const void* q, const void* kv, const int32_t* indices, void* 
     p.timeout_ns = g_timeout_ns.load();
     cudaError_t e;
     if (H <= 16)
-      e = fp8 ? launch_fwd<16, true>(p, s, st) : launch_fwd<16, false>(p, s, st);
+      e = multi ? (fp8 ? launch_fwd<16, true, true>(p, s, st) : launch_fwd<16, false, true>(p, s, st))
+                : (fp8 ? launch_fwd<16, true, false>(p, s, st) : launch_fwd<16, false, false>(p, s, st));
     else if (H == 32)
-      e = fp8 ? launch_fwd<32, true>(p, s, st) : launch_fwd<32, false>(p, s, st);
+      e = multi ? (fp8 ? launch_fwd<32, true, true>(p, s, st) : launch_fwd<32, false, true>(p, s, st))
+                : (fp8 ? launch_fwd<32, true, false>(p, s, st) : launch_fwd<32, false, false>(p, s, st));
     else
-      e = fp8 ? launch_fwd<64, true>(p, s, st) : launch_fwd<64, false>(p, s, st);
+      e = multi ? (fp8 ? launch_fwd<64, true, true>(p, s, st) : launch_fwd<64, false, true>(p, s, st))
+                : (fp8 ? launch_fwd<64, true, false>(p, s, st) : launch_fwd<64, false, false>(p, s, st));
     if (e != cudaSuccess) return GLM53_ERR_CUDA;
   }
   return GLM53_OK;
