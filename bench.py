@@ -468,7 +468,9 @@ def head_shard_leg(S, W, device, stream, dist, steps: int = 10) -> dict:
     """The north star's head-sharding sweep, on the MTP shape (C5: 128
     sequences x 4 tokens, top-k 2048, bf16 KV): rank r of N serves heads
     [r * 64 / N, (r + 1) * 64 / N) of the same batch, index lists and pool
-    replicated (vLLM TP). Times, max over ranks, launched eagerly:
+    replicated (vLLM TP). Times per step, max over ranks, from a CUDA graph of
+    `steps` steps (eager launches if the symmetric-memory barrier cannot be
+    captured; `timing` says which):
       kernel_ms    the op alone (this rank's heads, local output)
       nccl_ms      the op, then NCCL all_gather_into_tensor and the head
                    reorder copy into [T, 64, 512]
@@ -492,7 +494,8 @@ def head_shard_leg(S, W, device, stream, dist, steps: int = 10) -> dict:
     res = {"workload": "C5 MTP: 128 seqs x 4 tokens, topk 2048, ctx 32768, bf16 KV",
            "tokens": sets[0].T, "heads_total": 64, "heads_per_gpu": h, "n_gpus": world,
            "kv_bytes_per_gpu": sets[0].n_valid() * 1024}
-    res["kernel_ms"] = round(dist.max(eager_ms(kstep, steps, stream), device), 5)
+    res["kernel_ms"] = round(dist.max(graph_ms(kstep, steps, stream), device), 5)
+    res["timing"] = {"kernel": "graph"}
     if world == 1:
         res["fused_ms"] = res["kernel_ms"]
     else:
@@ -501,13 +504,29 @@ def head_shard_leg(S, W, device, stream, dist, steps: int = 10) -> dict:
         def nstep(k):
             kstep(k)
             S.gather_heads(outs[k % 2], world, staging=staging)
-        res["nccl_ms"] = round(dist.max(eager_ms(nstep, steps, stream), device), 5)
+        res["nccl_ms"] = round(dist.max(graph_ms(nstep, steps, stream), device), 5)
+        res["timing"]["nccl"] = "graph"
         gather = S.HeadShardGather(sets[0].T, 64, device=device)
 
         def fstep(k):
             w = sets[k % 2]
             gather(qs[k % 2], w.kv, w.indices, w.sm_scale, w.kv_scale)
-        res["fused_ms"] = round(dist.max(eager_ms(fstep, steps, stream), device), 5)
+
+        # diagnostic: the fused kernel without the closing barrier (not a
+        # usable result on its own: nothing orders the peers' stores yet)
+        def fstep_nb(k):
+            w = sets[k % 2]
+            gather(qs[k % 2], w.kv, w.indices, w.sm_scale, w.kv_scale, barrier=False)
+        res["fused_no_barrier_ms"] = round(dist.max(graph_ms(fstep_nb, steps, stream), device), 5)
+        dist.barrier()
+        try:
+            t_fused, how = graph_ms(fstep, steps, stream), "graph"
+        except RuntimeError:
+            torch.cuda.synchronize()
+            dist.barrier()
+            t_fused, how = eager_ms(fstep, steps, stream), "eager"
+        res["fused_ms"] = round(dist.max(t_fused, device), 5)
+        res["timing"]["fused"] = how
         dist.barrier()
         del gather
     res["value"] = round(sets[0].T / (res["fused_ms"] / 1e3), 1)
