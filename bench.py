@@ -82,7 +82,8 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--op", choices=["attention", "cache_write", "indexer", "topk", "decode_step"],
+    ap.add_argument("--op", choices=["attention", "paged", "cache_write", "indexer", "topk",
+                                     "decode_step"],
                     default="attention",
                     help="attention (the headline), the latent KV-cache writer, the indexer's "
                          "fp8 paged logits, its per-row top-k, or the four chained as one "
@@ -905,6 +906,80 @@ def topk_desc(args) -> dict:
             "rows_per_step": args.rows, "ctx": args.ctx, "topk": TOPK_K}
 
 
+def paged_sets(device, n_sets: int, seed0: int = 1100):
+    """C2-shaped decode batches in vLLM's form: 32 sequences (one request
+    each, context 8192 = 128 blocks of 64 over a 2048-block pool), request-local
+    top-2048 positions in a 2176-column buffer, as the indexer fills it."""
+    out = []
+    for s in range(n_sets):
+        rng = np.random.default_rng(seed0 + s)
+        T, ctx, n_blocks, width = 32, 8192, 2048, 2176
+        bt = np.stack([rng.permutation(n_blocks)[:ctx // 64] for _ in range(T)]).astype(np.int32)
+        pos = np.full((T, width), -1, np.int32)
+        for t in range(T):
+            pos[t, :2048] = rng.choice(ctx, 2048, replace=False)
+        q = torch.from_numpy(rng.standard_normal((T, 64, 512), dtype=np.float32)).to(torch.bfloat16)
+        from glm53_sparse_mla import workloads as W
+        kv = W.device_pool(n_blocks * 64, seed0 + s, device)
+        out.append((q.to(device), kv, torch.from_numpy(pos).to(device),
+                    torch.arange(T, dtype=torch.int32, device=device), torch.from_numpy(bt).to(device)))
+    return out
+
+
+def run_paged(args, dist: Dist):
+    """--op paged: the attention in vLLM's index form. The fused path
+    (sparse_fwd_paged: request-local positions converted to slots inside the
+    kernel's index compaction) against the sequence the reference backend runs
+    (its backend.py:341-348, 371-378): narrowing copy of the position buffer,
+    vLLM's triton_convert_req_index_to_global_index, then sparse_fwd. Both in
+    CUDA graphs over rotating input sets; the line's value is the fused path's."""
+    torch.cuda.set_device(dist.local)
+    device = torch.device("cuda", dist.local)
+    dist.init("nccl")
+    import glm53_sparse_mla as G
+    sets = paged_sets(device, max(1, args.sets))
+    outs = [torch.empty_like(s[0]) for s in sets]
+    scale = 512 ** -0.5
+
+    def fused(k):
+        q, kv, pos, req, bt = sets[k % len(sets)]
+        G.sparse_fwd_paged(q, kv, pos, req, bt, 64, scale, topk=2048, out=outs[k % len(sets)])
+
+    stream = torch.cuda.Stream(device)
+    ms_local, ms, clocks = time_graph(fused, args, dist, device, stream)
+    unfused_ms = None
+    try:
+        from vllm.v1.attention.backends.mla.sparse_utils import (
+            triton_convert_req_index_to_global_index as convert)
+        narrow = [torch.empty(s[2].shape[0], 2048, dtype=torch.int32, device=device) for s in sets]
+
+        def unfused(k):
+            q, kv, pos, req, bt = sets[k % len(sets)]
+            narrow[k % len(sets)].copy_(pos[:, :2048])
+            slots = convert(req, bt, narrow[k % len(sets)], BLOCK_SIZE=64, NUM_TOPK_TOKENS=2048)
+            torch.ops.glm53_sparse_mla.sparse_fwd(q, kv, slots, scale, 1.0, outs[k % len(sets)])
+        unfused_ms = round(graph_ms(unfused, min(args.steps, 50), stream), 5)
+    except Exception as e:  # vLLM or Triton unavailable on this host
+        unfused_ms = f"unavailable: {type(e).__name__}: {e}"[:200]
+    if dist.rank == 0:
+        T = sets[0][0].shape[0]
+        line = {"metric": f"sparse-MLA {UNIT}, paged index form (C2 batch)",
+                "value": round(T * dist.world / (ms / 1e3), 1), "unit": UNIT,
+                "n_gpus": dist.world, "steps": args.steps, "warmup": max(args.warmup, 3),
+                "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
+                "config": {"workload": "32 decode sequences x 8192 context, 64 heads, top-2048 "
+                                       "request-local positions (2176-column buffer), block 64",
+                           "parallelism": f"dp{dist.world}",
+                           "timing": "K steps in one CUDA graph, CUDA events, max over ranks"},
+                "unfused_ms_per_step": unfused_ms,
+                "unfused": "narrowing copy + vLLM triton_convert_req_index_to_global_index + "
+                           "sparse_fwd (the reference backend's sequence)",
+                "gpu_launches": args.steps, "clocks": clocks}
+        print(json.dumps(line), flush=True)
+    dist.close()
+
+
 def run_topk(args, dist: Dist):
     torch.cuda.set_device(dist.local)
     device = torch.device("cuda", dist.local)
@@ -1482,6 +1557,11 @@ def main():
                               "--op attention, cache_write, indexer and topk"}), flush=True)
         else:
             run_decode_step(args, dist)
+    elif args.op == "paged":
+        if args.impl == "reference":
+            run_reference(args, dist)
+        else:
+            run_paged(args, dist)
     elif args.op == "indexer":
         if args.impl == "reference":
             run_indexer_reference(args, dist)
