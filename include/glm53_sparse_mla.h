@@ -141,6 +141,23 @@ int glm53_sparse_mla_fwd_heads_gather(const void* q, const void* kv, const int32
                                       void* stream);
 
 /*
+ * Copy this rank's heads [head_offset, head_offset + heads) of `tokens`
+ * tokens from src, a bf16 [tokens, heads_total, 512] buffer, into the same
+ * place of each buffer in dsts (n_dsts device pointers, 0..8; an entry equal
+ * to src is skipped). One cudaMemcpy2DAsync per destination on `stream`, so
+ * the copy engines move the data (over NVLink for peer buffers) without SMs.
+ * It reads only src, which is local, and writes the destinations.
+ * This is the exchange step of the chunked head gather (glm53_sparse_mla.
+ * sharding.HeadShardGather, mode "copy"): each wave's attention output is
+ * pushed to the peers while the next wave computes.
+ * Replaces, like glm53_sparse_mla_fwd_heads_gather, the output all-gather a
+ * tensor-parallel caller would run after the reference op.
+ */
+int glm53_copy_head_slices(void* const* dsts, int n_dsts, const void* src, int64_t tokens,
+                           int64_t heads_total, int64_t head_offset, int64_t heads,
+                           void* stream);
+
+/*
  * As glm53_sparse_mla_fwd_ws, with the index list in vLLM's request-local
  * form: topk_positions[t][k] (row stride positions_row_stride >= topk, only
  * the first topk columns read) is a token position within request

@@ -57,6 +57,30 @@ def test_multi_output_epilogue_matches_plain_op(shape, kv_dtype):
         assert (rest == SENTINEL).all(), "heads outside this rank's slice were written"
 
 
+def test_copy_head_slices_places_one_ranks_heads():
+    """glm53_copy_head_slices: this rank's head slice of every token lands in
+    the same place of each destination; other heads and the source itself
+    are untouched."""
+    import ctypes
+    lib = ctypes.CDLL(G.library_path())
+    f = lib.glm53_copy_head_slices
+    f.restype = ctypes.c_int
+    f.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                  ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p]
+    T, total, off, h = 37, 64, 16, 16
+    src = torch.randn(T, total, 512, device="cuda").to(torch.bfloat16)
+    dsts = [torch.full((T, total, 512), SENTINEL, dtype=torch.bfloat16, device="cuda") for _ in range(2)]
+    keep = src.clone()
+    arr = (ctypes.c_void_p * 3)(dsts[0].data_ptr(), src.data_ptr(), dsts[1].data_ptr())
+    assert f(arr, 3, src.data_ptr(), T, total, off, h, torch.cuda.current_stream().cuda_stream) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(src, keep)
+    for d in dsts:
+        assert torch.equal(d[:, off:off + h], src[:, off:off + h])
+        assert (d[:, :off] == SENTINEL).all() and (d[:, off + h:] == SENTINEL).all()
+    assert f(arr, 3, src.data_ptr(), T, total, 56, h, None) == 1      # heads past the buffer
+
+
 def test_op_rejects_bad_arguments():
     w = W.config_c1(device="cuda")
     buf = torch.empty(w.T, 64, 512, dtype=torch.bfloat16, device="cuda")
@@ -86,16 +110,16 @@ def _rank_main(rank: int, world: int, port: int, result_path: str):
     try:
         full = W.config_c2(device="cuda", seed=31)
         ref = G.sparse_fwd(full.q, full.kv, full.indices, full.sm_scale)
-        gather = S.HeadShardGather(full.T, 64)
         q = S.shard_heads(full.q, rank, world)
-        for _ in range(2):                  # twice: the buffer is reused
-            out = gather(q, full.kv, full.indices, full.sm_scale)
-            torch.cuda.synchronize()
-            ok = torch.equal(out, ref)
-            if not ok:
-                break
-        torch.distributed.barrier()
-        del gather
+        ok = True
+        for mode, chunk in (("fused", None), ("copy", None), ("copy", 7)):
+            gather = S.HeadShardGather(full.T, 64, mode=mode, chunk_tokens=chunk)
+            for _ in range(2):              # twice: the buffer is reused
+                out = gather(q, full.kv, full.indices, full.sm_scale)
+                torch.cuda.synchronize()
+                ok = ok and torch.equal(out, ref)
+            torch.distributed.barrier()
+            del gather
     finally:
         with open(f"{result_path}.{rank}", "w") as f:
             f.write("ok" if ok else "mismatch")

@@ -1618,6 +1618,28 @@ extern "C" int glm53_sparse_mla_fwd_heads_gather(
                         stream, nullptr, &os);
 }
 
+extern "C" int glm53_copy_head_slices(void* const* dsts, int n_dsts, const void* src,
+                                      int64_t tokens, int64_t heads_total, int64_t head_offset,
+                                      int64_t heads, void* stream) {
+  if (dsts == nullptr || n_dsts < 0 || n_dsts > kMaxOutputs || src == nullptr || tokens < 0 ||
+      heads_total <= 0 || head_offset < 0 || heads <= 0 || head_offset + heads > heads_total)
+    return GLM53_ERR_RANK;
+  if (tokens == 0) return GLM53_OK;
+  const size_t row = static_cast<size_t>(kDim) * 2;                      // bytes per (token, head)
+  const size_t pitch = static_cast<size_t>(heads_total) * row;           // bytes per token
+  const size_t off = static_cast<size_t>(head_offset) * row;
+  for (int i = 0; i < n_dsts; ++i) {
+    if (dsts[i] == nullptr) return GLM53_ERR_ALIGN;
+    if (dsts[i] == src) continue;
+    if (cudaMemcpy2DAsync(static_cast<uint8_t*>(dsts[i]) + off, pitch,
+                          static_cast<const uint8_t*>(src) + off, pitch,
+                          static_cast<size_t>(heads) * row, static_cast<size_t>(tokens),
+                          cudaMemcpyDeviceToDevice, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+      return GLM53_ERR_CUDA;
+  }
+  return GLM53_OK;
+}
+
 // ---------------------------------------------------------------------------
 // No-allocation entry point
 // ---------------------------------------------------------------------------

@@ -105,11 +105,20 @@ class HeadShardGather:
     orders every rank's stores before anyone reads; the call returns this
     rank's gathered buffer. The buffer is reused by the next call.
 
+    ``mode="copy"`` exchanges the outputs with the copy engines instead: the
+    batch runs as one attention launch per wave of ``chunk_tokens`` tokens
+    (default: the SM count) into this rank's own buffer, and after each launch
+    a side stream pushes that chunk's head slice into every peer's buffer
+    (``glm53_copy_head_slices``: 2-D copies that read only local memory), so
+    a wave's exchange overlaps the next wave's compute and no SM stalls on
+    NVLink stores.
+
     Collective: every rank of ``group`` constructs it and calls it in the
     same order.
     """
 
-    def __init__(self, tokens: int, heads_total: int, group=None, device=None):
+    def __init__(self, tokens: int, heads_total: int, group=None, device=None,
+                 mode: str = "fused", chunk_tokens: int | None = None):
         import torch.distributed as dist
         import torch.distributed._symmetric_memory as symm_mem
 
@@ -125,15 +134,59 @@ class HeadShardGather:
         self.buf = symm_mem.empty(tokens, heads_total, 512, dtype=torch.bfloat16, device=device)
         self.handle = symm_mem.rendezvous(self.buf, self.group.group_name)
         self.ptrs = peer_pointer_order(self.handle.buffer_ptrs, self.rank)
+        if mode not in ("fused", "copy"):
+            raise ValueError(f"mode must be 'fused' or 'copy', got {mode!r}")
+        self.mode = mode
+        if mode == "copy":
+            import ctypes
+
+            from . import library_path
+            self._lib = ctypes.CDLL(library_path())
+            self._lib.glm53_copy_head_slices.restype = ctypes.c_int
+            self._lib.glm53_copy_head_slices.argtypes = [
+                ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p]
+            self._copy_stream = torch.cuda.Stream(device)
+            sms = torch.cuda.get_device_properties(device).multi_processor_count
+            self.chunk = int(chunk_tokens or sms)
+            self._row_bytes = heads_total * 512 * 2
 
     def __call__(self, q_shard: torch.Tensor, kv: torch.Tensor, indices: torch.Tensor,
                  sm_scale: float, kv_scale: float = 1.0, barrier: bool = True) -> torch.Tensor:
         if q_shard.shape[0] != self.tokens or q_shard.shape[1] != self.heads:
             raise ValueError(f"q shard must be [{self.tokens}, {self.heads}, 512], got "
                              f"{tuple(q_shard.shape)}")
-        torch.ops.glm53_sparse_mla.sparse_fwd_gather_heads(
-            q_shard, kv, indices, float(sm_scale), float(kv_scale), self.ptrs, self.rank,
-            self.head_offset, self.buf)
+        if self.mode == "fused":
+            torch.ops.glm53_sparse_mla.sparse_fwd_gather_heads(
+                q_shard, kv, indices, float(sm_scale), float(kv_scale), self.ptrs, self.rank,
+                self.head_offset, self.buf)
+        else:
+            self._chunked(q_shard, kv, indices, float(sm_scale), float(kv_scale))
         if barrier:
             self.handle.barrier(channel=0, timeout_ms=10000)
         return self.buf
+
+    def _chunked(self, q_shard, kv, indices, sm_scale, kv_scale):
+        import ctypes
+
+        main = torch.cuda.current_stream()
+        side = self._copy_stream
+        side.wait_stream(main)              # earlier readers of the buffers are done
+        dsts = (ctypes.c_void_p * len(self.ptrs))()
+        for t0 in range(0, self.tokens, self.chunk):
+            t1 = min(self.tokens, t0 + self.chunk)
+            out = self.buf[t0:t1]
+            torch.ops.glm53_sparse_mla.sparse_fwd_gather_heads(
+                q_shard[t0:t1], kv, indices[t0:t1], sm_scale, kv_scale, [out.data_ptr()], 0,
+                self.head_offset, out)
+            ev = torch.cuda.Event()
+            ev.record(main)
+            side.wait_event(ev)
+            for i, ptr in enumerate(self.ptrs):
+                dsts[i] = ptr + t0 * self._row_bytes
+            rc = self._lib.glm53_copy_head_slices(
+                dsts, len(self.ptrs), out.data_ptr(), t1 - t0, self.heads_total,
+                self.head_offset, self.heads, side.cuda_stream)
+            if rc != 0:
+                raise RuntimeError(f"glm53_copy_head_slices failed with status {rc}")
+        main.wait_stream(side)
