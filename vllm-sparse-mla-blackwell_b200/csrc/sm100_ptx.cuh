@@ -212,6 +212,20 @@ __device__ __forceinline__ float4 ldg_cg_f4(const void* p) {
   return v;
 }
 
+__device__ __forceinline__ void stg_cg_v4u(void* p, uint4 v) {
+  asm volatile("st.global.cg.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+__device__ __forceinline__ uint4 ldg_cg_v4u(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+
 __device__ __forceinline__ void stg_cg_f32(float* p, float v) {
   asm volatile("st.global.cg.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
 }

@@ -8,8 +8,11 @@
 //   cluster and each takes a contiguous chunk of the token's index list; their
 //   partial results are merged at the end of the same launch, either through a
 //   global workspace that stays in L2 (glm53_sparse_mla_fwd_ws, the torch op,
-//   the no-allocation entry point) or through distributed shared memory
+//   the no-allocation entry point; at 32 and 64 heads the partials cross it as
+//   f16 of each CTA's normalised output) or through distributed shared memory
 //   (glm53_sparse_mla_fwd, no global scratch).
+//   Before its grid-dependency wait a CTA prefetches its q rows and index
+//   chunk into L2, so those loads overlap the previous grid's tail.
 //
 // Per CTA (384 threads, one CTA per SM, ~222 KB shared memory)
 //   warps 0-3   softmax, GEMM2 issue, epilogue (warp w owns TMEM lanes 32w..)
@@ -110,7 +113,8 @@ struct Lay {
   static constexpr uint32_t kSmBar = kSmHead + 4 * 64 * 4;         // mbarriers
   static constexpr uint32_t kSmMisc = kSmBar + 24 * 8;             // tmem base, counts, abort flag
   static constexpr uint32_t kSmMlRecv = kSmMisc + 64;              // m[8][64], l[8][64] of the peers
-  static constexpr uint32_t kSmUsed = kSmMlRecv + 2 * 8 * 64 * 4;
+  static constexpr uint32_t kSmFlags = kSmMlRecv + 2 * 8 * 64 * 4;    // f16-overflow flag per peer
+  static constexpr uint32_t kSmUsed = kSmFlags + 8 * 4;
   static constexpr uint32_t kSmemBytes = kSmUsed + 1024;           // + slack to align the base
   static_assert(kSmemBytes <= 232448, "shared memory per block");
   static_assert(kSmKV % 1024 == 0 && kSmP % 1024 == 0, "swizzle atoms need 1024-byte bases");
@@ -246,7 +250,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
   constexpr int kStages = L::kStages;
   constexpr uint32_t kSmQ = L::kSmQ, kSmKV = L::kSmKV, kSmP = L::kSmP, kPBytes = L::kPBytes;
   constexpr uint32_t kSmIdx = L::kSmIdx, kSmHead = L::kSmHead, kSmBar = L::kSmBar;
-  constexpr uint32_t kSmMisc = L::kSmMisc, kSmMlRecv = L::kSmMlRecv;
+  constexpr uint32_t kSmMisc = L::kSmMisc, kSmMlRecv = L::kSmMlRecv, kSmFlags = L::kSmFlags;
   constexpr uint32_t kQRows = L::kQRows, kQBlock = L::kQBlock;
   // KV ring slot of tile t (S and P stay double-buffered: t & 1)
   auto stage_of = [](int t) -> int { return kStages == 2 ? (t & 1) : t % kStages; };
@@ -293,6 +297,19 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
   if (warp == kMmaWarp) {
     tmem_alloc(sb + kSmMisc + 4 * kMiscTmem, kTmemCols);
     tmem_relinquish();
+  }
+  if (warp == kMmaWarp - 1 && lane == 0) {
+    // L2 prefetch (a hint: it returns nothing, so it may precede the grid
+    // dependency wait) of this CTA's share of q and of its index chunk
+    const uint32_t qb = static_cast<uint32_t>(p.H) * kDim * 2u;
+    const uint32_t qs = qb / static_cast<uint32_t>(p.splits);
+    prefetch_l2_bulk(reinterpret_cast<const uint8_t*>(p.q) + static_cast<size_t>(token) * qb +
+                         static_cast<size_t>(split) * qs, qs);
+    const int k0p = split * p.chunk;
+    const int lenp = max(0, min(p.chunk, p.topk - k0p));
+    const uintptr_t a0 = reinterpret_cast<uintptr_t>(p.idx + static_cast<size_t>(token) * p.idx_stride + k0p);
+    const uintptr_t lo = (a0 + 15u) & ~uintptr_t(15), hi = (a0 + 4u * lenp) & ~uintptr_t(15);
+    if (hi > lo) prefetch_l2_bulk(reinterpret_cast<const void*>(lo), static_cast<uint32_t>(hi - lo));
   }
   __syncthreads();   // barriers initialised before anyone arrives on them
   // With programmatic dependent launch the set-up above overlaps the previous
@@ -748,6 +765,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
     if (has_head && half == 0) {
       m_sm[h] = n_tiles > 0 ? m_used : -INFINITY;
       l_sm[h] = n_tiles > 0 ? l_tot : 0.f;
+      f_sm[h] = (n_tiles > 0 && l_tot > 0.f) ? 1.f / l_tot : 0.f;   // the f16 split-merge partials' scale
     }
   }
 
@@ -794,10 +812,21 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
     // work: warp w reads TMEM lane quadrant w & 3 and head half w >> 2 (at
     // NH = 16, warps 0-3 take all heads). Per-head (max, sum) pairs go to
     // every peer's shared memory (a few hundred bytes); the partials go to
-    // the workspace, per (token, CTA) one slice per destination CTA laid out
-    // [NH / 4][dspan][4] floats, so a warp's 16-byte stores and loads cover
-    // 512 contiguous bytes. Every slice is written before the cluster barrier
-    // and read after it, so the workspace needs no initialisation.
+    // the workspace, per (token, CTA) one slice per destination CTA. Every
+    // slice is written before a cluster barrier and read after it, so the
+    // workspace needs no initialisation.
+    //
+    // At 32 and 64 heads a partial is sent as f16 of this CTA's own
+    // normalised output O / l (laid out [NH / 8][dspan][8], a warp's 16-byte
+    // stores and loads cover 512 contiguous bytes): half the bytes of fp32,
+    // and O / l is a convex combination of the gathered rows, so it fits
+    // f16's range unless the cache itself holds values beyond it. A CTA that
+    // meets such a value (or a non-finite one) raises a flag beside its
+    // (max, sum); if any CTA of the cluster did, all of them resend their
+    // unnormalised fp32 partials ([NH / 4][dspan][4] floats) behind a second
+    // barrier. At 16 heads (a quarter of the bytes) the partials are always
+    // fp32: there the flag's extra block barrier costs more than it saves.
+    constexpr bool kF16Part = NH >= 32;
     constexpr int kHalf = NH >= 32 ? NH / 2 : NH;
     constexpr int kV = kHalf / 4;                   // float4 per (d, peer)
     const int dspan = kDim / nranks;
@@ -809,6 +838,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
     const uint32_t tcol = static_cast<uint32_t>(32 * qd) << 16;
     float* const scal = reinterpret_cast<float*>(gb + kSmIdx);   // e[8][NH], 1/L[NH]
     const float* const ml = reinterpret_cast<const float*>(gb + kSmMlRecv);   // m[8][64], l[8][64]
+    const float* const flags = reinterpret_cast<const float*>(gb + kSmFlags);   // [8]
     auto load_half = [=](int m, float (&o)[kHalf]) {
       const uint32_t ta = tmem + tcol + static_cast<uint32_t>(m * NH + h0);
       if constexpr (kHalf == 32) {
@@ -817,6 +847,49 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
         tmem_ld_32x32b_x16(ta, o);
       }
       tmem_wait_ld();
+    };
+    // This CTA's partials for every other CTA's d-slice: f16 of O / l (returns
+    // whether a value left f16's finite range) or fp32 O.
+    auto send_partials = [&](auto f16_c) -> bool {
+      constexpr bool kF16 = decltype(f16_c)::value;
+      bool ovf = false;
+      if (!active) return ovf;
+#pragma unroll 1
+      for (int m = 0; m < 4; ++m) {
+        const int d = 128 * m + 32 * qd + lane;
+        const int owner = d / dspan;               // warp-uniform (dspan >= 64)
+        if (owner == split) continue;
+        float o[kHalf];
+        load_half(m, o);
+        if (n_tiles == 0) {
+#pragma unroll
+          for (int j = 0; j < kHalf; ++j) o[j] = 0.f;
+        }
+        const int dl = d - owner * dspan;
+        if constexpr (kF16) {
+          __half* const dst = reinterpret_cast<__half*>(ws_tok + static_cast<size_t>(split) * blk) +
+                              static_cast<size_t>(owner) * NH * dspan;
+#pragma unroll
+          for (int c = 0; c < kHalf / 8; ++c) {
+            uint32_t w[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float a = o[8 * c + 2 * k] * f_sm[h0 + 8 * c + 2 * k];
+              const float b = o[8 * c + 2 * k + 1] * f_sm[h0 + 8 * c + 2 * k + 1];
+              ovf |= !(fabsf(a) <= 65504.f) || !(fabsf(b) <= 65504.f);
+              w[k] = pack_f16x2(a, b);
+            }
+            stg_cg_v4u(dst + (static_cast<size_t>(h0 / 8 + c) * dspan + dl) * 8, make_uint4(w[0], w[1], w[2], w[3]));
+          }
+        } else {
+          float* const dst = ws_tok + static_cast<size_t>(split) * blk + static_cast<size_t>(owner) * NH * dspan;
+#pragma unroll
+          for (int c = 0; c < kV; ++c)
+            stg_cg_f4(dst + (static_cast<size_t>(h0 / 4 + c) * dspan + dl) * 4,
+                      make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]));
+        }
+      }
+      return ovf;
     };
 
     if (n_tiles > 0) mbar_wait_bounded(bar(kBarODone), (n_tiles - 1) & 1, abort_flag, p.timeout_ns);
@@ -830,28 +903,20 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
         st_dsmem_f32(mapa_shared(a + 4u * 8u * 64u, q), lv);
       }
     }
-    if (active) {
-#pragma unroll 1
-      for (int m = 0; m < 4; ++m) {
-        const int d = 128 * m + 32 * qd + lane;
-        const int owner = d / dspan;               // warp-uniform (dspan >= 64)
-        if (owner == split) continue;
-        float o[kHalf];
-        load_half(m, o);
-        if (n_tiles == 0) {
-#pragma unroll
-          for (int j = 0; j < kHalf; ++j) o[j] = 0.f;
-        }
-        float* const dst = ws_tok + static_cast<size_t>(split) * blk + static_cast<size_t>(owner) * NH * dspan;
-        const int dl = d - owner * dspan;
-#pragma unroll
-        for (int c = 0; c < kV; ++c)
-          stg_cg_f4(dst + (static_cast<size_t>(h0 / 4 + c) * dspan + dl) * 4,
-                    make_float4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]));
-      }
+    bool wide = !kF16Part;   // fp32 partials; cluster-uniform
+    if constexpr (kF16Part) {
+      const bool ovf = __syncthreads_or(send_partials(std::true_type{}));
+      if (tid < nranks)
+        st_dsmem_f32(mapa_shared(sb + kSmFlags + 4u * static_cast<uint32_t>(split), tid), ovf ? 1.f : 0.f);
+      __threadfence();
+      cluster_sync_all();   // every CTA's (max, sum), flag and f16 partials visible
+      for (int r = 0; r < nranks; ++r) wide |= flags[r] != 0.f;   // every CTA reads the same flags
     }
-    __threadfence();
-    cluster_sync_all();   // every CTA's (max, sum) and workspace stores visible
+    if (wide) {
+      send_partials(std::false_type{});
+      __threadfence();
+      cluster_sync_all();   // every CTA's (max, sum) and fp32 partials visible
+    }
     if (tid < NH) {
       float M = -INFINITY;
       for (int r = 0; r < nranks; ++r)
@@ -860,7 +925,8 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
       for (int r = 0; r < nranks; ++r) {
         const float lr = ml[512 + r * 64 + tid];
         const float e = lr > 0.f ? exp2f(ml[r * 64 + tid] - M) : 0.f;
-        scal[r * NH + tid] = e;
+        // a peer's f16 partial is O / l, its fp32 partial and this CTA's TMEM are O
+        scal[r * NH + tid] = (!wide && r != split) ? e * lr : e;
         L += lr * e;
       }
       scal[8 * NH + tid] = L > 0.f ? kvs / L : 0.f;
@@ -878,37 +944,72 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
 #pragma unroll 1
         for (int hp = 0; hp < kHalf; hp += 16) {
           const int hb = h0 + hp;
-          const float* const src0 = ws_tok + static_cast<size_t>(split) * NH * dspan +
-                                    static_cast<size_t>(hb / 4) * dspan * 4 + dl * 4;
           float o[16];
           tmem_ld_32x32b_x16(tmem + tcol + static_cast<uint32_t>(m * NH + hb), o);
           tmem_wait_ld();
 #pragma unroll
           for (int j = 0; j < 16; ++j) o[j] = n_tiles > 0 ? o[j] * scal[split * NH + hb + j] : 0.f;
-          // peers in batches of three, each batch's loads issued together
+          if (!wide) {
+            const __half* const src0 = reinterpret_cast<const __half*>(ws_tok) + static_cast<size_t>(split) * NH * dspan +
+                                       static_cast<size_t>(hb / 8) * dspan * 8 + dl * 8;
+            // peers in batches of three, each batch's loads issued together
 #pragma unroll 1
-          for (int i0 = 0; i0 < nranks - 1; i0 += 3) {
-            float4 v[3][4];
+            for (int i0 = 0; i0 < nranks - 1; i0 += 3) {
+              uint4 v[3][2];
 #pragma unroll
-            for (int i = 0; i < 3; ++i) {
-              const int r = i0 + i < split ? i0 + i : i0 + i + 1;
-              if (i0 + i < nranks - 1) {
+              for (int i = 0; i < 3; ++i) {
+                const int r = i0 + i < split ? i0 + i : i0 + i + 1;
+                if (i0 + i < nranks - 1) {
 #pragma unroll
-                for (int c = 0; c < 4; ++c)
-                  v[i][c] = ldg_cg_f4(src0 + static_cast<size_t>(r) * blk + static_cast<size_t>(c) * dspan * 4);
+                  for (int c = 0; c < 2; ++c)
+                    v[i][c] = ldg_cg_v4u(src0 + static_cast<size_t>(r) * blk * 2 + static_cast<size_t>(c) * dspan * 8);
+                }
+              }
+#pragma unroll
+              for (int i = 0; i < 3; ++i) {
+                const int r = i0 + i < split ? i0 + i : i0 + i + 1;
+                if (i0 + i < nranks - 1) {
+                  const float* e = scal + r * NH + hb;
+#pragma unroll
+                  for (int c = 0; c < 2; ++c) {
+                    const uint32_t w[4] = {v[i][c].x, v[i][c].y, v[i][c].z, v[i][c].w};
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[k]));
+                      o[8 * c + 2 * k] += f.x * e[8 * c + 2 * k];
+                      o[8 * c + 2 * k + 1] += f.y * e[8 * c + 2 * k + 1];
+                    }
+                  }
+                }
               }
             }
+          } else {
+            const float* const src0 = ws_tok + static_cast<size_t>(split) * NH * dspan +
+                                      static_cast<size_t>(hb / 4) * dspan * 4 + dl * 4;
+#pragma unroll 1
+            for (int i0 = 0; i0 < nranks - 1; i0 += 3) {
+              float4 v[3][4];
 #pragma unroll
-            for (int i = 0; i < 3; ++i) {
-              const int r = i0 + i < split ? i0 + i : i0 + i + 1;
-              if (i0 + i < nranks - 1) {
-                const float* e = scal + r * NH + hb;
+              for (int i = 0; i < 3; ++i) {
+                const int r = i0 + i < split ? i0 + i : i0 + i + 1;
+                if (i0 + i < nranks - 1) {
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                  o[4 * c] += v[i][c].x * e[4 * c];
-                  o[4 * c + 1] += v[i][c].y * e[4 * c + 1];
-                  o[4 * c + 2] += v[i][c].z * e[4 * c + 2];
-                  o[4 * c + 3] += v[i][c].w * e[4 * c + 3];
+                  for (int c = 0; c < 4; ++c)
+                    v[i][c] = ldg_cg_f4(src0 + static_cast<size_t>(r) * blk + static_cast<size_t>(c) * dspan * 4);
+                }
+              }
+#pragma unroll
+              for (int i = 0; i < 3; ++i) {
+                const int r = i0 + i < split ? i0 + i : i0 + i + 1;
+                if (i0 + i < nranks - 1) {
+                  const float* e = scal + r * NH + hb;
+#pragma unroll
+                  for (int c = 0; c < 4; ++c) {
+                    o[4 * c] += v[i][c].x * e[4 * c];
+                    o[4 * c + 1] += v[i][c].y * e[4 * c + 1];
+                    o[4 * c + 2] += v[i][c].z * e[4 * c + 2];
+                    o[4 * c + 3] += v[i][c].w * e[4 * c + 3];
+                  }
                 }
               }
             }
