@@ -918,16 +918,25 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_mla_fwd_kernel(const __gri
       cluster_sync_all();   // every CTA's (max, sum) and fp32 partials visible
     }
     if (tid < NH) {
+      // every rank's (max, sum) loaded at once (unrolled over the largest
+      // cluster), then combined
+      float mr[8], lr[8];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        mr[r] = r < nranks ? ml[r * 64 + tid] : 0.f;
+        lr[r] = r < nranks ? ml[512 + r * 64 + tid] : 0.f;
+      }
       float M = -INFINITY;
-      for (int r = 0; r < nranks; ++r)
-        if (ml[512 + r * 64 + tid] > 0.f) M = fmaxf(M, ml[r * 64 + tid]);
+#pragma unroll
+      for (int r = 0; r < 8; ++r)
+        if (lr[r] > 0.f) M = fmaxf(M, mr[r]);
       float L = 0.f;
-      for (int r = 0; r < nranks; ++r) {
-        const float lr = ml[512 + r * 64 + tid];
-        const float e = lr > 0.f ? exp2f(ml[r * 64 + tid] - M) : 0.f;
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const float e = lr[r] > 0.f ? exp2f(mr[r] - M) : 0.f;
         // a peer's f16 partial is O / l, its fp32 partial and this CTA's TMEM are O
-        scal[r * NH + tid] = (!wide && r != split) ? e * lr : e;
-        L += lr * e;
+        if (r < nranks) scal[r * NH + tid] = (!wide && r != split) ? e * lr[r] : e;
+        L += lr[r] * e;
       }
       scal[8 * NH + tid] = L > 0.f ? kvs / L : 0.f;
       if (split == 0 && p.lse != nullptr && tid < p.H)
