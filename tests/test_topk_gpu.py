@@ -46,6 +46,12 @@ def _logits(rows, width, seed, kind="normal", stride=None):
         x[:, ::7] = float("-inf")
         x[::3, 5] = float("nan")
         x[1::3, 11] = float("inf")
+    elif kind == "heavy":
+        # every 15th value positive, the rest exactly 0: for rows longer than
+        # about 15k the k-th largest is a 0 shared by more keys than the
+        # candidate buffer holds
+        x = torch.zeros((rows, stride))
+        x[:, ::15] = torch.randn((rows, (stride + 14) // 15), generator=g).abs() + 1.0
     return x.to(DEV)
 
 
@@ -93,6 +99,37 @@ def test_prefill_rows(kind):
     out = torch.empty((rows, k), dtype=torch.int32, device=DEV)
     G.top_k_per_row_prefill(logits, torch.from_numpy(starts).to(DEV), torch.from_numpy(ends).to(DEV),
                             out, rows, logits.stride(0), 1, k)
+    torch.cuda.synchronize()
+    _check(out, logits, starts, ends, k)
+
+
+@pytest.mark.parametrize("kind", ["normal", "ties", "special", "heavy"])
+@pytest.mark.parametrize("rows,width", [(32, 20000), (60, 40000), (5, 131072)])
+def test_cluster_rows(rows, width, kind):
+    """Batches small enough for a cluster of CTAs per row (on a 148-SM part:
+    4 CTAs per row at 32 and 5 rows, 2 at 60 rows), rows of 12K values and
+    more: decode rows of ragged lengths (short ones, exactly k, k + 1, the
+    full width), then prefill rows at unaligned offsets."""
+    k = 2048
+    rng = np.random.default_rng(rows * 7 + len(kind))
+    seq = rng.integers(1, width + 1, rows).astype(np.int32)
+    seq[0] = width
+    seq[1] = k
+    seq[2] = k + 1
+    seq[3] = 100
+    logits = _logits(rows, width, seed=rows + width, kind=kind)
+    out = torch.full((rows, k), -9, dtype=torch.int32, device=DEV)
+    G.top_k_per_row_decode(logits, 1, torch.from_numpy(seq).to(DEV), out, rows, logits.stride(0), 1, k)
+    torch.cuda.synchronize()
+    _check(out, logits, np.zeros(rows, np.int64), seq.astype(np.int64), k)
+
+    starts = rng.integers(0, width // 3, rows).astype(np.int32)
+    starts[0] = 0
+    ends = np.minimum(starts.astype(np.int64) + rng.integers(1, width, rows), width).astype(np.int32)
+    ends[0] = width
+    out = torch.full((rows, k), -9, dtype=torch.int32, device=DEV)
+    G.top_k_per_row_prefill(logits, torch.from_numpy(starts).to(DEV), torch.from_numpy(ends).to(DEV), out, rows,
+                            logits.stride(0), 1, k)
     torch.cuda.synchronize()
     _check(out, logits, starts, ends, k)
 

@@ -129,13 +129,14 @@ __device__ __forceinline__ void find_digit(const uint32_t* hist, int nb, uint32_
 // find_digit over the first digit, reading the kHists per-warp histogram
 // copies directly: thread t sums bins 4t..4t+3 of every copy (one 16-byte
 // load per copy), which saves a merge pass and its barrier.
+template <int NC = kHists>
 __device__ __forceinline__ void find_digit0(const uint32_t* whist, uint32_t need, uint32_t* wsum,
                                             uint32_t* ctl) {
   static_assert(kBins0 == 4 * kThreads, "four first-digit bins per thread");
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   uint32_t c[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-  for (int w = 0; w < kHists; ++w) {
+  for (int w = 0; w < NC; ++w) {
     const uint4 v = *reinterpret_cast<const uint4*>(whist + w * kBins0 + 4 * tid);
     c[0] += v.x;
     c[1] += v.y;
@@ -206,13 +207,72 @@ __device__ __forceinline__ void block_scan2(uint32_t a, uint32_t b, uint32_t* sc
   __syncthreads();   // scratch may be reused right after
 }
 
-__global__ void __launch_bounds__(kThreads, 1) topk_per_row_kernel(const Params p) {
-  // Programmatic dependent launch: the logits come from the previous kernel
-  // in the stream, so wait for it before any global access; dependents may
-  // launch at once (they wait in turn for this grid to finish).
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  extern __shared__ __align__(16) uint32_t smem[];
+// The k_rem largest of the threshold bin's keys (bits 20..0 still open),
+// from the n candidates (keys and positions) held in shared memory, written
+// to out_c[0, k_rem) (n_above of them strictly above the final prefix first,
+// then the first k_rem - n_above equal to it). Every thread of the block
+// calls it; hist and whist are free scratch (2048 words each).
+__device__ __forceinline__ void finish_candidates(const uint32_t* cand_key, const uint32_t* cand_pos,
+                                                  uint32_t c0_count, uint32_t d0, int k, uint32_t n_gt0,
+                                                  uint32_t k_rem, int32_t* out_c, uint32_t* hist,
+                                                  uint32_t* whist, uint32_t* wsum, uint32_t* wcnt,
+                                                  uint32_t* ctl) {
+  const int tid = threadIdx.x;
+  // two digits over bits 20..0 (bits 20..11 in 1024 bins, then 10..0 in
+  // 2048), each with its own histogram, zeroed together up front. ctl and
+  // wsum are rewritten only after the next pass's first barrier, which every
+  // thread reaches after reading them, so a pass needs no closing barrier.
+  uint32_t prefix = d0 << 21, mask = 0xFFE00000u;
+  bool settled = c0_count == k_rem;
+  const int n = static_cast<int>(c0_count);
+  if (!settled) {
+    for (int i = tid; i < kBins0; i += kThreads) {
+      hist[i] = 0;
+      whist[i] = 0;
+    }
+    __syncthreads();
+  }
+#pragma unroll 1
+  for (int pss = 0; pss < 2 && !settled; ++pss) {
+    const int shift = pss == 0 ? 11 : 0;
+    const uint32_t width = pss == 0 ? 0x3FFu : 0x7FFu;
+    uint32_t* const h = pss == 0 ? hist : whist;
+    for (int i = tid; i < n; i += kThreads) {
+      const uint32_t u = cand_key[i];
+      if ((u & mask) == prefix) atomicAdd(&h[(u >> shift) & width], 1u);
+    }
+    __syncthreads();
+    find_digit(h, static_cast<int>(width) + 1, k_rem, wsum, ctl);
+    prefix |= ctl[0] << shift;
+    mask |= width << shift;
+    k_rem -= ctl[1];
+    settled = ctl[2] == k_rem;
+  }
+  // candidates above the prefix, then the first k_rem equal to it: per-thread
+  // counts over a strided share of the candidates and a block scan
+  const uint32_t n_above = static_cast<uint32_t>(k) - n_gt0 - k_rem;
+  uint32_t ng = 0, ne = 0;
+  for (int i = tid; i < n; i += kThreads) {
+    const uint32_t u = cand_key[i] & mask;
+    ng += u > prefix;
+    ne += u == prefix;
+  }
+  uint32_t og, oe, tg, te;
+  block_scan2(ng, ne, wcnt, og, oe, tg, te);
+  for (int i = tid; i < n; i += kThreads) {
+    const uint32_t u = cand_key[i] & mask;
+    if (u > prefix) {
+      out_c[og++] = static_cast<int32_t>(cand_pos[i]);
+    } else if (u == prefix) {
+      if (oe < k_rem) out_c[n_above + oe] = static_cast<int32_t>(cand_pos[i]);
+      ++oe;
+    }
+  }
+}
+
+// One row by one CTA (every thread of the block), shared memory `smem` of
+// kSmemBytes: the whole algorithm, rows of any length.
+__device__ __forceinline__ void topk_row_single(const Params& p, long long row, uint32_t* smem) {
   uint32_t* const keys_raw = smem;                               // [kChunk + 4]
   uint32_t* const whist = smem + kChunk + 4;                     // [kHists][kBins0]
   uint32_t* const hist = whist + kHists * kBins0;                // [kBins0]
@@ -223,7 +283,6 @@ __global__ void __launch_bounds__(kThreads, 1) topk_per_row_kernel(const Params 
   uint32_t* const ctl = wcnt + 4 * kWarps;                       // [8]
   const uint32_t bar = static_cast<uint32_t>(__cvta_generic_to_shared(ctl + 8));
 
-  const long long row = blockIdx.x;
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   long long start, end;
@@ -426,58 +485,7 @@ __global__ void __launch_bounds__(kThreads, 1) topk_per_row_kernel(const Params 
   // ---- the k_rem largest of the threshold bin's keys (bits 20..0 still open)
   int32_t* const out_c = out + n_gt0;
   if (keep) {
-    // candidates in shared memory: two digits over bits 20..0 (bits 20..11
-    // in 1024 bins, then 10..0 in 2048), each with its own histogram (the
-    // merged first-digit histogram and the first per-warp copy, both free
-    // now), zeroed together up front. ctl and wsum are rewritten only after
-    // the next pass's first barrier, which every thread reaches after
-    // reading them, so a pass needs no closing barrier.
-    uint32_t prefix = d0 << 21, mask = 0xFFE00000u;
-    bool settled = c0_count == k_rem;
-    const int n = static_cast<int>(c0_count);
-    if (!settled) {
-      for (int i = tid; i < kBins0; i += kThreads) {
-        hist[i] = 0;
-        whist[i] = 0;
-      }
-      __syncthreads();
-    }
-#pragma unroll 1
-    for (int pss = 0; pss < 2 && !settled; ++pss) {
-      const int shift = pss == 0 ? 11 : 0;
-      const uint32_t width = pss == 0 ? 0x3FFu : 0x7FFu;
-      uint32_t* const h = pss == 0 ? hist : whist;
-      for (int i = tid; i < n; i += kThreads) {
-        const uint32_t u = cand_key[i];
-        if ((u & mask) == prefix) atomicAdd(&h[(u >> shift) & width], 1u);
-      }
-      __syncthreads();
-      find_digit(h, static_cast<int>(width) + 1, k_rem, wsum, ctl);
-      prefix |= ctl[0] << shift;
-      mask |= width << shift;
-      k_rem -= ctl[1];
-      settled = ctl[2] == k_rem;
-    }
-    // candidates above the prefix, then the first k_rem equal to it: per-thread
-    // counts over a strided share of the candidates and a block scan
-    const uint32_t n_above = static_cast<uint32_t>(k) - n_gt0 - k_rem;
-    uint32_t ng = 0, ne = 0;
-    for (int i = tid; i < n; i += kThreads) {
-      const uint32_t u = cand_key[i] & mask;
-      ng += u > prefix;
-      ne += u == prefix;
-    }
-    uint32_t og, oe, tg, te;
-    block_scan2(ng, ne, wcnt, og, oe, tg, te);
-    for (int i = tid; i < n; i += kThreads) {
-      const uint32_t u = cand_key[i] & mask;
-      if (u > prefix) {
-        out_c[og++] = static_cast<int32_t>(cand_pos[i]);
-      } else if (u == prefix) {
-        if (oe < k_rem) out_c[n_above + oe] = static_cast<int32_t>(cand_pos[i]);
-        ++oe;
-      }
-    }
+    finish_candidates(cand_key, cand_pos, c0_count, d0, k, n_gt0, k_rem, out_c, hist, whist, wsum, wcnt, ctl);
     return;
   }
 
@@ -550,6 +558,292 @@ __global__ void __launch_bounds__(kThreads, 1) topk_per_row_kernel(const Params 
   }
 }
 
+__global__ void __launch_bounds__(kThreads, 1) topk_per_row_kernel(const Params p) {
+  // Programmatic dependent launch: the logits come from the previous kernel
+  // in the stream, so wait for it before any global access; dependents may
+  // launch at once (they wait in turn for this grid to finish).
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  extern __shared__ __align__(16) uint32_t smem[];
+  topk_row_single(p, blockIdx.x, smem);
+}
+
+// ---------------------------------------------------------------------------
+// Small batches: one row over a cluster of C CTAs
+// ---------------------------------------------------------------------------
+// A decode batch has few rows (32 at a 32-sequence decode step), so one CTA
+// per row leaves most SMs idle while each row's load, histogram and
+// compaction run on one SM. Here C CTAs (a thread-block cluster) share a row:
+// CTA c loads, keys, histograms and compacts slice c of it (len / C values),
+// and the cluster exchanges the few words it must through distributed shared
+// memory:
+//   1. every CTA sends its 11-bit histogram to CTA 0; CTA 0 finds the
+//      threshold bin d0 and sends (d0, count above, count in d0) back;
+//   2. every CTA counts its positions above d0 and in d0 and sends the two
+//      counts to all; each writes its positions above d0 at its offset and
+//      sends its candidates (keys in d0 with positions) to CTA 0;
+//   3. CTA 0 resolves the candidates alone (finish_candidates).
+// A row longer than C slices, or whose threshold bin holds more than kCand
+// keys (heavy ties), is done by CTA 0 alone with the one-CTA algorithm.
+constexpr int kSlice = 32 * 1024;   // values per CTA slice
+// shared memory of the cluster kernel (words, as laid out there): it also
+// holds the one-CTA layout (kSmemBytes) for the rows CTA 0 does alone
+template <int C>
+constexpr size_t cluster_smem_bytes() {
+  return sizeof(uint32_t) * (kSlice + 4 + kHists * kBins0 + C * kBins0 + 2 * kCand + 4 * kWarps + 8 + 16 + 2) + 16;
+}
+static_assert(cluster_smem_bytes<4>() <= 232448, "cluster top-k shared memory");
+static_assert(cluster_smem_bytes<2>() >= kSmemBytes, "room for the one-CTA layout");
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
+               : "=r"(r)
+               : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void st_cluster_u32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint4 v) {
+  asm volatile("st.shared::cluster.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+
+template <int C>
+__global__ void __launch_bounds__(kThreads, 1) topk_cluster_kernel(const Params p) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  extern __shared__ __align__(16) uint32_t smem[];
+  const long long row = blockIdx.x / C;
+  const uint32_t rank = blockIdx.x % C;   // clusters are C consecutive CTAs: the cluster rank
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  long long start, end;
+  if (p.seq_lens != nullptr) {
+    start = 0;
+    end = static_cast<long long>(p.seq_lens[row / p.next_n]) - p.next_n + row % p.next_n + 1;
+  } else {
+    start = p.row_starts[row];
+    end = p.row_ends[row];
+  }
+  const long long len = end > start ? end - start : 0;
+  int32_t* const out = p.out + row * p.out_stride;
+  const int k = p.k;
+  // (every CTA of the cluster takes the same branch: the same row)
+  if (len <= k) {
+    if (rank == 0)
+      for (int i = tid; i < k; i += kThreads) out[i] = i < len ? i : -1;
+    return;
+  }
+  if (len > static_cast<long long>(C) * kSlice) {
+    if (rank == 0) topk_row_single(p, row, smem);
+    return;
+  }
+
+  uint32_t* const keys_raw = smem;                       // [kSlice + 4]
+  uint32_t* const whist = keys_raw + kSlice + 4;         // [kHists][kBins0]
+  uint32_t* const rhist = whist + kHists * kBins0;       // [C][kBins0]: CTA 0 receives every slice's histogram
+  uint32_t* const cand_key = rhist + C * kBins0;         // [kCand]: CTA 0 receives the candidates
+  uint32_t* const cand_pos = cand_key + kCand;           // [kCand]
+  uint32_t* const wcnt = cand_pos + kCand;               // [4][kWarps]
+  uint32_t* const wsum = wcnt + 2 * kWarps;              // [kWarps] (scan scratch)
+  uint32_t* const ctl = wcnt + 4 * kWarps;               // [8]: d0, count above d0, count in d0 (from CTA 0)
+  uint32_t* const cnt = ctl + 8;                         // [2][8]: each CTA's counts above / in d0
+  const uint32_t bar = static_cast<uint32_t>(__cvta_generic_to_shared(cnt + 16));
+
+  const long long per = (len + C - 1) / C;
+  const long long s0 = static_cast<long long>(rank) * per;
+  const long long slen = s0 < len ? (len - s0 < per ? len - s0 : per) : 0;
+  const float* const src = p.logits + row * p.stride0 + start + s0;
+  const uint32_t head = static_cast<uint32_t>(((16u - (reinterpret_cast<uintptr_t>(src) & 15u)) & 15u) >> 2);
+  const int off = static_cast<int>((4u - head) & 3u);
+  uint32_t* const keys = keys_raw + off;
+
+  uint32_t* const my_hist = whist + (warp % kHists) * kBins0;
+  for (int i = tid; i < kHists * kBins0; i += kThreads) whist[i] = 0;
+  if (tid == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  // the slice: its 16-byte aligned interior by one bulk copy, its ragged
+  // ends (< 4 values each) by plain loads
+  if (slen > 0) {
+    const long long h = head < slen ? head : slen;
+    const long long body = ((slen - h) / 4) * 4;
+    if (tid == 0) {
+      const uint32_t bytes = static_cast<uint32_t>(body * 4);
+      asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+                   : "memory");
+      if (bytes > 0)
+        asm volatile(
+            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                static_cast<uint32_t>(__cvta_generic_to_shared(keys + h))),
+            "l"(src + h), "r"(bytes), "r"(bar)
+            : "memory");
+    }
+    if (tid < h) keys[tid] = __float_as_uint(src[tid]);
+    const long long tail0 = h + body;
+    if (tid < slen - tail0) keys[tail0 + tid] = __float_as_uint(src[tail0 + tid]);
+    uint32_t done = 0;
+    const uint64_t t0 = now_ns();
+    while (true) {
+      asm volatile(
+          "{\n\t.reg .pred q;\n\tmbarrier.try_wait.parity.acquire.cta.shared::cta.b64 q, [%1], 0;\n\t"
+          "selp.u32 %0, 1, 0, q;\n\t}"
+          : "=r"(done)
+          : "r"(bar)
+          : "memory");
+      if (done) break;
+      if (now_ns() - t0 > p.timeout_ns) {
+        if (tid == 0) atomicOr(&g_topk_status, kStatusTimeout);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  // keys in place and this slice's first-digit histogram (16-byte sweeps as
+  // in the one-CTA algorithm; keys_raw words [off, off + slen) hold the slice)
+  const int W = off + static_cast<int>(slen);
+#pragma unroll 1
+  for (int s = 0; s < W; s += 16 * kThreads) {
+    const int base = s + 512 * warp + 4 * lane;
+    uint4 v[4] = {};
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      if (base + 128 * q < W) v[q] = *reinterpret_cast<const uint4*>(keys_raw + base + 128 * q);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int a = base + 128 * q;
+      if (a < W) {
+        uint32_t w[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          w[c] = order_key(__uint_as_float(w[c]));
+          if (a + c >= off && a + c < W) atomicAdd(&my_hist[w[c] >> 21], 1u);
+        }
+        if (a >= off && a + 4 <= W) {
+          *reinterpret_cast<uint4*>(keys_raw + a) = make_uint4(w[0], w[1], w[2], w[3]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            if (a + c >= off && a + c < W) keys_raw[a + c] = w[c];
+        }
+      }
+    }
+  }
+  __syncthreads();
+  // 1. this slice's histogram (its kHists copies summed) into CTA 0's rhist[rank]
+  {
+    uint4 h4 = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+    for (int w = 0; w < kHists; ++w) {
+      const uint4 v = *reinterpret_cast<const uint4*>(whist + w * kBins0 + 4 * tid);
+      h4.x += v.x;
+      h4.y += v.y;
+      h4.z += v.z;
+      h4.w += v.w;
+    }
+    st_cluster_v4(cluster_addr(rhist + rank * kBins0 + 4 * tid, 0), h4);
+  }
+  cluster_sync_all();
+  if (rank == 0) {
+    find_digit0<C>(rhist, static_cast<uint32_t>(k), wsum, ctl);
+    if (tid < C)
+      for (int j = 0; j < 3; ++j) st_cluster_u32(cluster_addr(ctl + j, tid), ctl[j]);
+  }
+  cluster_sync_all();
+  const uint32_t d0 = ctl[0];
+  const uint32_t n_gt0 = ctl[1];
+  const uint32_t c0_count = ctl[2];
+  const uint32_t k_rem = static_cast<uint32_t>(k) - n_gt0;
+  const bool keep = c0_count <= static_cast<uint32_t>(kCand);
+  if (!keep && c0_count != k_rem) {
+    // heavy ties in the threshold bin: the whole row by CTA 0 (no further
+    // access to another CTA's shared memory by anyone)
+    if (rank == 0) topk_row_single(p, row, smem);
+    return;
+  }
+  // 2. positions above d0 and in d0: per-thread counts over this slice, a
+  // block scan, the block totals to every CTA
+  uint32_t ng = 0, ne = 0;
+#pragma unroll 1
+  for (int s = 0; s < W; s += 16 * kThreads) {
+    const int base = s + 512 * warp + 4 * lane;
+    uint4 v[4] = {};
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      if (base + 128 * q < W) v[q] = *reinterpret_cast<const uint4*>(keys_raw + base + 128 * q);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int a = base + 128 * q;
+      const uint32_t w[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const bool ok = a + c >= off && a + c < W;
+        const uint32_t dg = w[c] >> 21;
+        ng += ok && dg > d0;
+        ne += ok && dg == d0;
+      }
+    }
+  }
+  uint32_t og, oe, tg, te;
+  block_scan2(ng, ne, wcnt, og, oe, tg, te);
+  if (tid < C) {
+    st_cluster_u32(cluster_addr(cnt + rank, tid), tg);
+    st_cluster_u32(cluster_addr(cnt + 8 + rank, tid), te);
+  }
+  cluster_sync_all();
+  for (uint32_t r = 0; r < rank; ++r) {
+    og += cnt[r];
+    oe += cnt[8 + r];
+  }
+#pragma unroll 1
+  for (int s = 0; s < W; s += 16 * kThreads) {
+    const int base = s + 512 * warp + 4 * lane;
+    uint4 v[4] = {};
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      if (base + 128 * q < W) v[q] = *reinterpret_cast<const uint4*>(keys_raw + base + 128 * q);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int a = base + 128 * q;
+      const uint32_t w[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        if (a + c < off || a + c >= W) continue;
+        const uint32_t u = w[c];
+        const uint32_t dg = u >> 21;
+        const int32_t pos = static_cast<int32_t>(s0 + (a + c - off));
+        if (dg > d0) {
+          out[og++] = pos;
+        } else if (dg == d0) {
+          if (keep) {
+            st_cluster_u32(cluster_addr(cand_key + oe, 0), u);
+            st_cluster_u32(cluster_addr(cand_pos + oe, 0), static_cast<uint32_t>(pos));
+          } else {
+            out[n_gt0 + oe] = pos;   // the whole bin is taken
+          }
+          ++oe;
+        }
+      }
+    }
+  }
+  cluster_sync_all();   // every candidate in CTA 0; no shared-memory access across CTAs after this
+  // 3. the candidates, by CTA 0 (rhist and whist are free scratch now)
+  if (rank == 0 && keep)
+    finish_candidates(cand_key, cand_pos, c0_count, d0, k, n_gt0, k_rem, out + n_gt0, rhist, whist, wsum, wcnt,
+                      ctl);
+}
+
 // Launch with programmatic stream serialization, so this grid may begin
 // launching while the previous kernel in the stream drains; the kernel's
 // griddepcontrol.wait, before its first global access, keeps the order.
@@ -570,6 +864,40 @@ cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t 
 }
 
 bool g_attr_set[64] = {};
+int g_sm_count[64] = {};
+
+// Cluster size for a batch: C CTAs per row while the batch then still fits
+// on the SMs at once and every row fits in C slices, else one CTA per row.
+// The cluster's synchronisation costs about 2 us per launch, which rows
+// shorter than about 12K values do not earn back (measured on a B200: at 32
+// rows, 8.8 vs 11.0 us at 8192 values, 11.4 vs 11.0 us at 12288, 17.1 vs
+// 11.8 us at 32768), so they keep one CTA per row.
+constexpr long long kClusterMinWidth = 12 * 1024;
+int cluster_ctas(long long num_rows, long long row_width, int sms) {
+  if (row_width < kClusterMinWidth) return 1;
+  if (num_rows * 4 <= sms && row_width <= 4ll * kSlice) return 4;
+  if (num_rows * 2 <= sms && row_width <= 2ll * kSlice) return 2;
+  return 1;
+}
+
+template <int C>
+cudaError_t launch_cluster(const Params& p, long long num_rows, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(num_rows * C));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = cluster_smem_bytes<C>();
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = C;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, topk_cluster_kernel<C>, p);
+}
 
 }  // namespace topk
 }  // namespace glm53
@@ -602,7 +930,12 @@ extern "C" int glm53_topk_per_row(const float* logits, int64_t num_rows, int64_t
   // any capture (the host call itself is not capturable).
   if (!g_attr_set[dev]) {
     if (cudaFuncSetAttribute(topk_per_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kSmemBytes)) != cudaSuccess)
+                             static_cast<int>(kSmemBytes)) != cudaSuccess ||
+        cudaFuncSetAttribute(topk_cluster_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(cluster_smem_bytes<2>())) != cudaSuccess ||
+        cudaFuncSetAttribute(topk_cluster_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(cluster_smem_bytes<4>())) != cudaSuccess ||
+        cudaDeviceGetAttribute(&g_sm_count[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
       return GLM53_ERR_CUDA;
     g_attr_set[dev] = true;
   }
@@ -618,10 +951,16 @@ extern "C" int glm53_topk_per_row(const float* logits, int64_t num_rows, int64_t
   p.out_stride = out_stride;
   p.k = topk;
   p.timeout_ns = 1000000000ull;
-  return launch_pdl(topk_per_row_kernel, dim3(static_cast<unsigned>(num_rows)), dim3(kThreads),
-                    kSmemBytes, static_cast<cudaStream_t>(stream), p) == cudaSuccess
-             ? GLM53_OK
-             : GLM53_ERR_CUDA;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int c = cluster_ctas(num_rows, stride0, g_sm_count[dev]);
+  cudaError_t e;
+  if (c == 4)
+    e = launch_cluster<4>(p, num_rows, st);
+  else if (c == 2)
+    e = launch_cluster<2>(p, num_rows, st);
+  else
+    e = launch_pdl(topk_per_row_kernel, dim3(static_cast<unsigned>(num_rows)), dim3(kThreads), kSmemBytes, st, p);
+  return e == cudaSuccess ? GLM53_OK : GLM53_ERR_CUDA;
 }
 
 extern "C" int glm53_topk_status(uint32_t* status, int clear) {
