@@ -36,6 +36,10 @@
 //      are written.
 // A row whose bin d0 holds more than kCand keys (heavy ties) resolves the
 // remaining bits with passes over the whole row instead.
+//
+// Small batches of long rows (12K values and more, up to 4 rows per 4 SMs)
+// share each row over a cluster of 2 or 4 CTAs instead (topk_cluster_kernel,
+// below): the same steps, each CTA on its slice of the row.
 
 #include <cuda_runtime.h>
 
