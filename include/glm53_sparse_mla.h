@@ -323,7 +323,11 @@ int glm53_concat_and_cache_status(uint32_t* status, int clear);
  * vllm/_custom_ops.py:2799-2840), which vLLM's sparse-attention indexer calls
  * to fill the topk_indices_buffer the reference's backend reads
  * (glm53_sparse_mla/backend.py:310-314 of the reference). 1 <= topk <= 16384.
- * The first call on a device sets the kernel's shared-memory size; make it
+ * A small batch of rows at least 12K values wide (stride0) runs each row on a
+ * cluster of 2 or 4 CTAs, otherwise each row on one CTA; the choice depends
+ * only on num_rows, stride0 and the device's SM count, so a captured launch
+ * stays valid for every replay of the same shapes.
+ * The first call on a device sets the kernels' shared-memory sizes; make it
  * before any stream capture. Asynchronous on `stream`; no allocation.
  */
 int glm53_topk_per_row(const float* logits, int64_t num_rows, int64_t stride0, int64_t stride1,
