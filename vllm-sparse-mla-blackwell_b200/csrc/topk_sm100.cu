@@ -59,6 +59,7 @@ constexpr int kHists = 4;                 // warp w adds into first-digit histog
 constexpr int kChunk = 32 * 1024;         // keys held in shared memory at a time (4 sweeps)
 constexpr int kCand = 4096;               // candidates (keys in the threshold bin) kept
 constexpr int kMaxTopk = 16384;
+constexpr long long kSpecMax = 16 * 1024;  // decode rows this wide are loaded before their length is known
 constexpr unsigned kStatusTimeout = 1u;
 
 __device__ unsigned int g_topk_status = 0;
@@ -289,8 +290,45 @@ __device__ __forceinline__ void topk_row_single(const Params& p, long long row, 
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
+  // The row goes through shared memory in chunks of kChunk values (a row
+  // that fits is loaded once): each chunk's 16-byte aligned interior by one
+  // bulk copy, its ragged ends (< 4 values each) by plain loads. kChunk is a
+  // multiple of 4, so every chunk starts at the same offset within 16 bytes,
+  // and `pad` puts its interior on a 16-byte boundary: keys[i] holds value
+  // c0 + i, converted to its key in place.
+  // A decode row starts at position 0, so when the logits rows are at most
+  // kSpecMax values wide the whole row is requested before its length is
+  // read: the length load and the row load overlap (one dependent L2 round
+  // trip fewer). Wider rows are not, since a row shorter than k would still
+  // have to wait for its copy to land before the CTA may exit.
+  const bool decode = p.seq_lens != nullptr;
+  const long long spec = decode && p.stride0 <= kSpecMax ? p.stride0 : 0;
+  auto head_of = [](const float* a) {
+    return static_cast<uint32_t>(((16u - (reinterpret_cast<uintptr_t>(a) & 15u)) & 15u) >> 2);
+  };
+  auto issue_copy = [&](const float* from, long long clen, uint32_t h0, uint32_t* to) {
+    // thread 0: the aligned interior of [from, from + clen) into to[h, ...)
+    const long long h = h0 < clen ? h0 : clen;
+    const uint32_t bytes = static_cast<uint32_t>(((clen - h) / 4) * 4 * 4);
+    asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+                 : "memory");
+    if (bytes > 0)
+      asm volatile(
+          "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+              static_cast<uint32_t>(__cvta_generic_to_shared(to + h))),
+          "l"(from + h), "r"(bytes), "r"(bar)
+          : "memory");
+  };
+  if (tid == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    if (spec > 0) {
+      const float* const r0 = p.logits + row * p.stride0;
+      issue_copy(r0, spec, head_of(r0), keys_raw + ((4u - head_of(r0)) & 3u));
+    }
+  }
   long long start, end;
-  if (p.seq_lens != nullptr) {
+  if (decode) {
     start = 0;
     end = static_cast<long long>(p.seq_lens[row / p.next_n]) - p.next_n + row % p.next_n + 1;
   } else {
@@ -300,45 +338,7 @@ __device__ __forceinline__ void topk_row_single(const Params& p, long long row, 
   const long long len = end > start ? end - start : 0;
   int32_t* const out = p.out + row * p.out_stride;
   const int k = p.k;
-  if (len <= k) {
-    for (int i = tid; i < k; i += kThreads) out[i] = i < len ? i : -1;
-    return;
-  }
-  const float* const src = p.logits + row * p.stride0 + start;
-  const bool one_chunk = len <= kChunk;
-
-  // The row goes through shared memory in chunks of kChunk values (a row
-  // that fits is loaded once): each chunk's 16-byte aligned interior by one
-  // bulk copy, its ragged ends (< 4 values each) by plain loads. kChunk is a
-  // multiple of 4, so every chunk starts at the same offset within 16 bytes,
-  // and `pad` puts its interior on a 16-byte boundary: keys[i] holds value
-  // c0 + i, converted to its key in place.
-  const uint32_t head = static_cast<uint32_t>(((16u - (reinterpret_cast<uintptr_t>(src) & 15u)) & 15u) >> 2);
-  uint32_t* const keys = keys_raw + ((4u - head) & 3u);
-  if (tid == 0) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar) : "memory");
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  __syncthreads();
-  uint32_t phase = 0;
-  auto load_chunk = [&](long long c0, long long clen) {
-    const long long h = head < clen ? head : clen;
-    const long long body = ((clen - h) / 4) * 4;
-    if (tid == 0) {
-      const uint32_t bytes = static_cast<uint32_t>(body * 4);
-      asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
-                   "r"(bytes)
-                   : "memory");
-      if (bytes > 0)
-        asm volatile(
-            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                static_cast<uint32_t>(__cvta_generic_to_shared(keys + h))),
-            "l"(src + c0 + h), "r"(bytes), "r"(bar)
-            : "memory");
-    }
-    if (tid < h) keys[tid] = __float_as_uint(src[c0 + tid]);
-    const long long tail0 = h + body;
-    if (tid < clen - tail0) keys[tail0 + tid] = __float_as_uint(src[c0 + tail0 + tid]);
+  auto wait_copy = [&](uint32_t parity) {
     uint32_t done = 0;
     const uint64_t t0 = now_ns();
     while (true) {
@@ -346,7 +346,7 @@ __device__ __forceinline__ void topk_row_single(const Params& p, long long row, 
           "{\n\t.reg .pred q;\n\tmbarrier.try_wait.parity.acquire.cta.shared::cta.b64 q, [%1], %2;\n\t"
           "selp.u32 %0, 1, 0, q;\n\t}"
           : "=r"(done)
-          : "r"(bar), "r"(phase)
+          : "r"(bar), "r"(parity)
           : "memory");
       if (done) break;
       if (now_ns() - t0 > p.timeout_ns) {
@@ -354,6 +354,41 @@ __device__ __forceinline__ void topk_row_single(const Params& p, long long row, 
         break;
       }
     }
+  };
+  if (len <= k) {
+    for (int i = tid; i < k; i += kThreads) out[i] = i < len ? i : -1;
+    if (tid == 0 && spec > 0) wait_copy(0);   // no copy may still target this CTA's shared memory
+    return;
+  }
+  const float* const src = p.logits + row * p.stride0 + start;
+  const bool one_chunk = len <= kChunk;
+  const uint32_t head = head_of(src);
+  uint32_t* const keys = keys_raw + ((4u - head) & 3u);
+  __syncthreads();
+  uint32_t phase = 0;
+  bool spec_left = spec > 0;   // the requested first chunk is consumed once (later passes reload)
+  auto load_chunk = [&](long long c0, long long clen) {
+    if (c0 == 0 && spec_left) {
+      spec_left = false;
+      // the decode row's first chunk, requested above for `spec` values:
+      // its ragged ends, then (an invalid row longer than stride0 only)
+      // whatever lies past it
+      const long long h = head < spec ? head : spec;
+      const long long tail0 = h + ((spec - h) / 4) * 4;
+      if (tid < h) keys[tid] = __float_as_uint(src[tid]);
+      if (tid < spec - tail0) keys[tail0 + tid] = __float_as_uint(src[tail0 + tid]);
+      for (long long i = spec + tid; i < clen; i += kThreads) keys[i] = __float_as_uint(src[i]);
+      wait_copy(phase);
+      phase ^= 1u;
+      __syncthreads();
+      return;
+    }
+    const long long h = head < clen ? head : clen;
+    const long long tail0 = h + ((clen - h) / 4) * 4;
+    if (tid == 0) issue_copy(src + c0, clen, head, keys);
+    if (tid < h) keys[tid] = __float_as_uint(src[c0 + tid]);
+    if (tid < clen - tail0) keys[tail0 + tid] = __float_as_uint(src[c0 + tail0 + tid]);
+    wait_copy(phase);
     phase ^= 1u;
     __syncthreads();
   };
