@@ -47,6 +47,7 @@
 
 #include <cmath>
 #include <cstdint>
+#include <atomic>
 #include <mutex>
 #include <utility>
 
@@ -430,16 +431,22 @@ bool make_kv_map(CUtensorMap* map, const Params& p) {
 
 template <int H, int NEXT_N>
 cudaError_t launch(const Params& p, const CUtensorMap& map, int B, cudaStream_t stream) {
-  static bool attr_set[64] = {};
+  // once per device and instantiation, under a lock (first calls may come
+  // from several host threads)
+  static std::atomic<bool> attr_set[64] = {};
+  static std::mutex attr_mutex;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    e = cudaFuncSetAttribute(indexer_logits_kernel<H, NEXT_N>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(Layout<H * NEXT_N>::kBytes));
-    if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
+  if (dev >= 0 && dev < 64 && !attr_set[dev].load(std::memory_order_acquire)) {
+    std::lock_guard<std::mutex> lock(attr_mutex);
+    if (!attr_set[dev].load(std::memory_order_relaxed)) {
+      e = cudaFuncSetAttribute(indexer_logits_kernel<H, NEXT_N>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(Layout<H * NEXT_N>::kBytes));
+      if (e != cudaSuccess) return e;
+      attr_set[dev].store(true, std::memory_order_release);
+    }
   }
   const int span = kTile * p.tiles_per_cta;
   const dim3 grid(static_cast<unsigned>((p.max_model_len + span - 1) / span),

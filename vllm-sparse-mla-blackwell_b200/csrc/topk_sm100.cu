@@ -43,7 +43,9 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
+#include <mutex>
 #include <utility>
 
 #include "glm53_sparse_mla.h"
@@ -902,7 +904,10 @@ cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t 
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
-bool g_attr_set[64] = {};
+// per-device set-up, done once under g_init_mutex (first calls may come
+// from several host threads)
+std::mutex g_init_mutex;
+std::atomic<bool> g_attr_set[64] = {};
 int g_sm_count[64] = {};
 
 // Cluster size for a batch: C CTAs per row while the batch then still fits
@@ -967,16 +972,19 @@ extern "C" int glm53_topk_per_row(const float* logits, int64_t num_rows, int64_t
   if (dev < 0 || dev >= 64) return GLM53_ERR_DEVICE;
   // Opt in to the large dynamic shared-memory size once per device, before
   // any capture (the host call itself is not capturable).
-  if (!g_attr_set[dev]) {
-    if (cudaFuncSetAttribute(topk_per_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kSmemBytes)) != cudaSuccess ||
-        cudaFuncSetAttribute(topk_cluster_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(cluster_smem_bytes<2>())) != cudaSuccess ||
-        cudaFuncSetAttribute(topk_cluster_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(cluster_smem_bytes<4>())) != cudaSuccess ||
-        cudaDeviceGetAttribute(&g_sm_count[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-      return GLM53_ERR_CUDA;
-    g_attr_set[dev] = true;
+  if (!g_attr_set[dev].load(std::memory_order_acquire)) {
+    std::lock_guard<std::mutex> lock(g_init_mutex);
+    if (!g_attr_set[dev].load(std::memory_order_relaxed)) {
+      if (cudaFuncSetAttribute(topk_per_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(kSmemBytes)) != cudaSuccess ||
+          cudaFuncSetAttribute(topk_cluster_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(cluster_smem_bytes<2>())) != cudaSuccess ||
+          cudaFuncSetAttribute(topk_cluster_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(cluster_smem_bytes<4>())) != cudaSuccess ||
+          cudaDeviceGetAttribute(&g_sm_count[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return GLM53_ERR_CUDA;
+      g_attr_set[dev].store(true, std::memory_order_release);
+    }
   }
   Params p;
   p.logits = logits;
