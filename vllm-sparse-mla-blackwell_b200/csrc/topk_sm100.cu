@@ -618,11 +618,12 @@ __global__ void __launch_bounds__(kThreads, 1) topk_per_row_kernel(const Params 
 // CTA c loads, keys, histograms and compacts slice c of it (len / C values),
 // and the cluster exchanges the few words it must through distributed shared
 // memory:
-//   1. every CTA sends its 11-bit histogram to CTA 0; CTA 0 finds the
-//      threshold bin d0 and sends (d0, count above, count in d0) back;
+//   1. CTA 0 reads every CTA's 11-bit histogram, finds the threshold bin d0
+//      and sends (d0, count above, count in d0) back;
 //   2. every CTA counts its positions above d0 and in d0 and sends the two
-//      counts to all; each writes its positions above d0 at its offset and
-//      sends its candidates (keys in d0 with positions) to CTA 0;
+//      counts to all; each writes its positions above d0 at its offset,
+//      stages its candidates (keys in d0 with positions) and then sends them
+//      to CTA 0 in one burst;
 //   3. CTA 0 resolves the candidates alone (finish_candidates).
 // A row longer than C slices, or whose threshold bin holds more than kCand
 // keys (heavy ties), is done by CTA 0 alone with the one-CTA algorithm.
@@ -651,6 +652,15 @@ __device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
 
 __device__ __forceinline__ void st_cluster_u32(uint32_t addr, uint32_t v) {
   asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint4 ld_cluster_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared::cluster.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
 }
 
 __device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint4 v) {
@@ -782,7 +792,9 @@ __global__ void __launch_bounds__(kThreads, 1) topk_cluster_kernel(const Params 
     }
   }
   __syncthreads();
-  // 1. this slice's histogram (its kHists copies summed) into CTA 0's rhist[rank]
+  // 1. this slice's histogram (its kHists copies summed) into its own rhist;
+  // after the barrier CTA 0 pulls every slice's histogram (each thread its
+  // four bins from every CTA, summed)
   {
     uint4 h4 = make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
@@ -793,11 +805,23 @@ __global__ void __launch_bounds__(kThreads, 1) topk_cluster_kernel(const Params 
       h4.z += v.z;
       h4.w += v.w;
     }
-    st_cluster_v4(cluster_addr(rhist + rank * kBins0 + 4 * tid, 0), h4);
+    *reinterpret_cast<uint4*>(rhist + 4 * tid) = h4;
   }
   cluster_sync_all();
   if (rank == 0) {
-    find_digit0<C>(rhist, static_cast<uint32_t>(k), wsum, ctl);
+    uint4 v[C];
+#pragma unroll
+    for (int r = 0; r < C; ++r) v[r] = ld_cluster_v4(cluster_addr(rhist + 4 * tid, r));
+    uint4 h4 = v[0];
+#pragma unroll
+    for (int r = 1; r < C; ++r) {
+      h4.x += v[r].x;
+      h4.y += v[r].y;
+      h4.z += v[r].z;
+      h4.w += v[r].w;
+    }
+    *reinterpret_cast<uint4*>(rhist + 4 * tid) = h4;   // this thread's bins only: no barrier needed
+    find_digit0<1>(rhist, static_cast<uint32_t>(k), wsum, ctl);
     if (tid < C)
       for (int j = 0; j < 3; ++j) st_cluster_u32(cluster_addr(ctl + j, tid), ctl[j]);
   }
@@ -843,9 +867,10 @@ __global__ void __launch_bounds__(kThreads, 1) topk_cluster_kernel(const Params 
     st_cluster_u32(cluster_addr(cnt + 8 + rank, tid), te);
   }
   cluster_sync_all();
+  uint32_t eq_base = 0;
   for (uint32_t r = 0; r < rank; ++r) {
     og += cnt[r];
-    oe += cnt[8 + r];
+    eq_base += cnt[8 + r];
   }
 #pragma unroll 1
   for (int s = 0; s < W; s += 16 * kThreads) {
@@ -868,14 +893,22 @@ __global__ void __launch_bounds__(kThreads, 1) topk_cluster_kernel(const Params 
           out[og++] = pos;
         } else if (dg == d0) {
           if (keep) {
-            st_cluster_u32(cluster_addr(cand_key + oe, 0), u);
-            st_cluster_u32(cluster_addr(cand_pos + oe, 0), static_cast<uint32_t>(pos));
+            cand_key[oe] = u;        // staged here, sent to CTA 0 after the pass
+            cand_pos[oe] = static_cast<uint32_t>(pos);
           } else {
-            out[n_gt0 + oe] = pos;   // the whole bin is taken
+            out[n_gt0 + eq_base + oe] = pos;   // the whole bin is taken
           }
           ++oe;
         }
       }
+    }
+  }
+  if (keep && rank != 0) {
+    // this slice's candidates to CTA 0 in one burst (CTA 0's own are in place)
+    __syncthreads();
+    for (uint32_t i = tid; i < te; i += kThreads) {
+      st_cluster_u32(cluster_addr(cand_key + eq_base + i, 0), cand_key[i]);
+      st_cluster_u32(cluster_addr(cand_pos + eq_base + i, 0), cand_pos[i]);
     }
   }
   cluster_sync_all();   // every candidate in CTA 0; no shared-memory access across CTAs after this
