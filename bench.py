@@ -367,13 +367,15 @@ def gather_roof_ms(G, sets, stream, n_steps: int):
 def extra_configs(args, G, W, device, stream, hbm_peak: float) -> dict:
     """The other benchmark configurations, timed the same way as the headline
     (a CUDA graph of back-to-back launches over rotating input sets, CUDA
-    events): C3 mixed prefill + decode, C4 fp8 decode, C5 MTP with bf16 and
-    fp8 KV. Each reports ms per step, query-tokens/s and the fraction of the
+    events): C3 mixed prefill + decode, C4 decode with fp8 KV (and the same
+    shape with bf16 KV, for the fp8-vs-bf16 comparison), C5 MTP with bf16
+    and fp8 KV. Each reports ms per step, query-tokens/s and the fraction of the
     HBM roofline (algorithmic bytes / time / measured copy bandwidth)."""
     out = {}
     for key, mk, n_sets, steps in (
             ("c3", lambda s: W.config_c3(device=device, seed=s), 2, 6),
             ("c4_fp8", lambda s: W.config_c4(device=device, seed=s), 8, 50),
+            ("c4_bf16", lambda s: W.config_c4(device=device, seed=s, kv_dtype="bf16"), 8, 50),
             ("c5_bf16", lambda s: W.config_c5(device=device, seed=s, heads=64), 2, 10),
             ("c5_fp8", lambda s: W.config_c5(device=device, seed=s, heads=64, kv_dtype="fp8"), 2, 10)):
         sets = [mk(200 + s) for s in range(n_sets)]

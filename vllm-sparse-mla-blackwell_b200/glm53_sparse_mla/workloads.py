@@ -255,10 +255,11 @@ def config_c3(device="cuda", seed: int = 3, heads: int = 32) -> Workload:
                     meta={"prefill_tokens": pre, "decode_tokens": n_dec})
 
 
-def config_c4(device="cuda", seed: int = 4, heads: int = 16) -> Workload:
+def config_c4(device="cuda", seed: int = 4, heads: int = 16, kv_dtype: str = "fp8") -> Workload:
     """fp8_e4m3 decode at long context: 64 sequences x 1 token, 16 heads, topk
     2048, context 65536, pool of 524288 fp8 slots with per-tensor scale 0.05,
-    ~2% -1 sentinels."""
+    ~2% -1 sentinels. ``kv_dtype="bf16"`` gives the same shape with a bf16
+    pool (the fp8-vs-bf16 comparison at this shape)."""
     rng = np.random.default_rng(seed)
     n_seq, ctx, n_blocks, K, scale = 64, 65536, 8192, 2048, 0.05
     ind = np.empty((n_seq, K), np.int32)
@@ -267,9 +268,10 @@ def config_c4(device="cuda", seed: int = 4, heads: int = 16) -> Workload:
         ind[s] = _paged_slots(rng, bt, rng.choice(ctx, K, replace=False))
     ind[rng.random(ind.shape) < 0.02] = -1
     q = _normal_bf16(rng, (n_seq, heads, D), device)
-    kv = device_pool(n_blocks * BLOCK, seed, device, "fp8", scale)
-    return Workload("c4_decode_fp8_long", q, kv, torch.from_numpy(ind).to(device), D ** -0.5,
-                    kv_scale=scale, meta={"n_seq": n_seq, "context": ctx})
+    kv = device_pool(n_blocks * BLOCK, seed, device, kv_dtype, scale)
+    name = "c4_decode_fp8_long" if kv_dtype == "fp8" else "c4_decode_bf16_long"
+    return Workload(name, q, kv, torch.from_numpy(ind).to(device), D ** -0.5,
+                    kv_scale=scale if kv_dtype == "fp8" else 1.0, meta={"n_seq": n_seq, "context": ctx})
 
 
 def config_c5(device="cuda", seed: int = 5, heads: int = 64, kv_dtype: str = "bf16",
