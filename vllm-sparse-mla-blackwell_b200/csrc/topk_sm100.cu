@@ -632,7 +632,7 @@ constexpr int kSlice = 32 * 1024;   // values per CTA slice
 // holds the one-CTA layout (kSmemBytes) for the rows CTA 0 does alone
 template <int C>
 constexpr size_t cluster_smem_bytes() {
-  return sizeof(uint32_t) * (kSlice + 4 + kHists * kBins0 + C * kBins0 + 2 * kCand + 4 * kWarps + 8 + 16 + 2) + 16;
+  return sizeof(uint32_t) * (kSlice + 4 + kHists * kBins0 + kBins0 + 2 * kCand + 4 * kWarps + 8 + 16 + 2) + 16;
 }
 static_assert(cluster_smem_bytes<4>() <= 232448, "cluster top-k shared memory");
 static_assert(cluster_smem_bytes<2>() >= kSmemBytes, "room for the one-CTA layout");
@@ -661,12 +661,6 @@ __device__ __forceinline__ uint4 ld_cluster_v4(uint32_t addr) {
                : "r"(addr)
                : "memory");
   return v;
-}
-
-__device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint4 v) {
-  asm volatile("st.shared::cluster.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
-               "r"(v.w)
-               : "memory");
 }
 
 template <int C>
@@ -701,8 +695,8 @@ __global__ void __launch_bounds__(kThreads, 1) topk_cluster_kernel(const Params 
 
   uint32_t* const keys_raw = smem;                       // [kSlice + 4]
   uint32_t* const whist = keys_raw + kSlice + 4;         // [kHists][kBins0]
-  uint32_t* const rhist = whist + kHists * kBins0;       // [C][kBins0]: CTA 0 receives every slice's histogram
-  uint32_t* const cand_key = rhist + C * kBins0;         // [kCand]: CTA 0 receives the candidates
+  uint32_t* const rhist = whist + kHists * kBins0;       // [kBins0]: this slice's histogram (CTA 0: the row's)
+  uint32_t* const cand_key = rhist + kBins0;             // [kCand]: this slice's candidates (CTA 0: the row's)
   uint32_t* const cand_pos = cand_key + kCand;           // [kCand]
   uint32_t* const wcnt = cand_pos + kCand;               // [4][kWarps]
   uint32_t* const wsum = wcnt + 2 * kWarps;              // [kWarps] (scan scratch)
