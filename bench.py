@@ -1338,6 +1338,25 @@ def run_decode_step(args, dist: Dist):
     stream = torch.cuda.Stream(device)
     ms_rank, ms_step, clocks = time_graph(step, args, dist, device, stream)
     value = args.rows * dist.world / (ms_step / 1e3)
+    # the same step with vLLM's compiled top-k in place of this repo's, timed
+    # the same way: inside the step a kernel's code is cold at every launch,
+    # which a graph of top-k launches alone does not show
+    vllm_cmp = None
+    if dist.world == 1:
+        try:
+            from vllm import _custom_ops as ops
+
+            def vstep(k):
+                d = sets[k % len(sets)]
+                G.concat_and_cache_mla(d["kv_new"], d["kv_new"][:, :0], d["lat"], d["slots"], "auto", one)
+                G.fp8_paged_mqa_logits(d["qi"], d["icache"], d["w"], ctx, d["bt"], args.ctx, logits=logits)
+                ops.top_k_per_row_decode(logits, 1, ctx, pos, args.rows, args.ctx, 1, TOPK_K)
+                G.sparse_fwd_paged(d["q"], d["lat"].view(-1, 512), pos, req, d["bt"], IDX_BLOCK,
+                                   512 ** -0.5, out=out)
+            ms_v, _, _ = time_graph(vstep, args, Dist(1), device, stream)
+            vllm_cmp = {"top_k": "vllm._custom_ops.top_k_per_row_decode", "ms_per_step": round(ms_v, 5)}
+        except Exception as exc:   # library code, optional
+            vllm_cmp = {"unavailable": repr(exc)[:120]}
     if dist.rank == 0:
         line = {"metric": f"sparse decode step query-tokens/s (cache write + indexer logits + "
                           f"top-{TOPK_K} + attention, ctx {args.ctx}, 64 heads)",
@@ -1353,6 +1372,8 @@ def run_decode_step(args, dist: Dist):
                            "rows": args.rows, "ctx": args.ctx, "parallelism": f"dp{dist.world}",
                            "timing": "K steps in one CUDA graph, CUDA events, max over ranks"},
                 "gpu_launches": 4 * args.steps, "clocks": clocks}
+        if vllm_cmp is not None:
+            line["library_comparison"] = vllm_cmp
         print(json.dumps(line), flush=True)
     dist.close()
 
